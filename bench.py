@@ -1,0 +1,366 @@
+"""Benchmark: talker decode seq-steps/s, B=64 ragged, on 1..8 B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = the whole talker decode step of 64 ragged sequences (contexts
+U[64, 2048], seeded), 28-layer random-init bf16 decoder (hidden 2048, 16/8
+heads, head_dim 128, FFN 6144, RoPE theta 1e6, codec vocab 3072), bf16 KV in
+16-token pages scattered over a 512k-token pool, GPU planner, fused sampler,
+commit - replayed from one CUDA graph.  Under torchrun each rank owns its own
+64 requests and page pool (request-sharded data parallelism, no collective on
+the data path); timing is the max over ranks (gloo for the scalar reduce).
+
+Reported on the JSON line besides the throughput:
+  e2e          the same metric through TalkerDecodeStep.step() with host
+               buffers: pinned H2D of the step inputs, replay, D2H of tokens;
+  roofline     the decode-attention launch (decode + merge kernels) timed
+               alone with CUDA events over the same metadata: algorithmic
+               KV + q + out bytes / duration vs the measured HBM copy peak;
+  cpu_baseline the CPU port of the step (oracle/talker_step.py) on a bounded
+               sample (rank 0, N = 1);
+  clocks       nvidia-smi samples taken during the timed region.
+``--impl reference`` times the CPU port alone (the reference arm).
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "talker decode seq-steps/s (B=64 ragged) at 1/2/4/8 B200; attn HBM GB/s vs peak"
+UNIT = "seq-steps/s"
+BATCH = 64
+CTX_LO, CTX_HI = 64, 2048
+POOL_TOKENS = 512 * 1024
+
+
+def parse() -> argparse.Namespace:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=300)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--layers", type=int, default=28, help="decoder layers (28 = BASELINE config 2)")
+    p.add_argument("--pool-tokens", type=int, default=POOL_TOKENS)
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks() -> tuple[float, str]:
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        return float(json.loads(f.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def contexts_for(rank: int) -> list[int]:
+    g = torch.Generator().manual_seed(1000 + rank)
+    return torch.randint(CTX_LO, CTX_HI + 1, (BATCH,), generator=g).tolist()
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device) -> None:
+        self.proc = None
+        self.target = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.target = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            self.target = str(device.index or 0)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.target, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in getattr(self, "lines", []):
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7], strict=True):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=600))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline(budget_s: float, layers: int) -> dict:
+    from oracle.talker_step import CpuTalkerStep
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    step = CpuTalkerStep(contexts=contexts_for(0), num_layers=layers)
+    step.time_step(layers=1)  # warm-up
+    runs = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or not runs:
+        runs.append(step.time_step(layers=1))
+    full = statistics.mean(r["full_step_s"] for r in runs)
+    return {
+        "value": BATCH / full,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": (f"{len(runs)} sampled steps of the CPU port (oracle/talker_step.py): host planner for all "
+                   f"{BATCH} rows, 1 of {layers} decoder layers and the head + sampler for all rows in fp32, "
+                   f"extrapolated linearly to {layers} layers; {full * 1e3:.0f} ms per full step"),
+    }
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from oracle.talker_step import CpuTalkerStep
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    step = CpuTalkerStep(contexts=contexts_for(0), num_layers=args.layers)
+    for _ in range(args.warmup):
+        step.time_step(layers=1)
+    probe = step.time_step(layers=1)["layers_s"] + 1e-3
+    # bound the whole run to a few minutes: sample rows when K steps of one layer would take too long
+    rows = BATCH
+    if probe * args.steps > 150.0:
+        rows = max(8, int(BATCH * 150.0 / (probe * args.steps)))
+    times = [step.time_step(rows=rows, layers=1)["full_step_s"] for _ in range(args.steps)]
+    per_step = statistics.mean(times)
+    value = BATCH / per_step
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": per_step * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (random-init weights, N(0,1) KV, seeded ragged contexts)",
+        "config": {"workload": "BASELINE config 2: talker decode step, B=64, ctx U[64,2048], 28 layers, "
+                               "P=16, 512k-token pool", "global_batch": BATCH, "seq_len": CTX_HI,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"each step: host planner for {BATCH} rows, 1 of {args.layers} layers and head + "
+                                   f"sampler for {rows} rows (fp32, CPU port), extrapolated to the full step"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    nqt = importlib.import_module("nari-qwen3-tts_b200")
+    from importlib import import_module
+
+    talker_step = import_module("nari-qwen3-tts_b200.talker_step")
+    lib_mod = import_module("nari-qwen3-tts_b200._lib")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    shape = talker_step.TalkerShape(num_layers=args.layers)
+    pages = args.pool_tokens // 16
+    step = talker_step.TalkerDecodeStep(shape=shape, batch=BATCH, total_pages=pages, page_size=16,
+                                        max_pages_per_seq=(CTX_HI + 1024) // 16, device=dev, seed=rank)
+    contexts = contexts_for(rank)
+    step.admit(contexts, scatter_seed=rank)
+    lib_mod.reset_launch_count()
+    step.capture(warmup=2)
+    launches_per_step = lib_mod.launch_count() // 3  # two eager warm-ups + the captured pass
+    executed = 2
+    for _ in range(args.warmup):
+        step.replay()
+    executed += args.warmup
+    torch.cuda.synchronize()
+
+    # ---------------------------------------------------------------- timed region
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            step.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    executed += args.steps
+    elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
+    value = world * BATCH * args.steps / (elapsed_ms / 1e3)
+
+    # ---------------------------------------------------------------- e2e through step()
+    g = torch.Generator().manual_seed(rank)
+    host_in = torch.randn(BATCH, shape.hidden, generator=g).to(torch.bfloat16)
+    step.step(host_in)
+    executed += 1
+    e2e_steps = max(20, args.steps // 2)
+    torch.cuda.synchronize()
+    barrier(world)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        step.step(host_in)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    executed += e2e_steps
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+    e2e_value = world * BATCH * e2e_steps / (e2e_ms / 1e3)
+
+    # ---------------------------------------------------------------- attention roofline
+    # the binding holds the metadata of the last executed step: every row at initial + executed tokens
+    lengths = [n + executed for n in contexts]
+    attn_bytes = sum(lengths) * 2 * shape.num_kv_heads * shape.head_dim * 2 + 2 * BATCH * shape.num_heads * shape.head_dim * 2
+    q = torch.randn(BATCH, shape.num_heads, shape.head_dim, device=dev).to(torch.bfloat16)
+    b = step.binding
+    outs = torch.empty(BATCH, shape.num_heads, shape.head_dim, dtype=torch.bfloat16, device=dev)
+
+    def attention_pass():
+        for layer in range(shape.num_layers):
+            nqt.batch_decode_paged(q, step.storage[layer], b.paged_kv_indptr, b.paged_kv_indices,
+                                   b.paged_kv_last_page_len, b.decode_workspace, batch_capacity=BATCH, out=outs,
+                                   plan=False)
+
+    attention_pass()
+    ag = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ag):
+        attention_pass()
+    for _ in range(3):
+        ag.replay()
+    reps = max(10, args.steps // 4)
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(reps):
+        ag.replay()
+    a1.record(stream)
+    torch.cuda.synchronize()
+    attn_ms = max_over_ranks(a0.elapsed_time(a1), world) / (reps * shape.num_layers)
+    peak, peak_kind = peaks()
+    achieved = attn_bytes / (attn_ms / 1e3) / 1e9
+    status = nqt.kernels.read_status(dev) | int(step.planner.status.item())
+
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init bf16 weights, N(0,1) KV, seeded ragged contexts)",
+        "config": {
+            "workload": f"BASELINE config 2: talker decode step, B={BATCH} ragged ctx U[{CTX_LO},{CTX_HI}], "
+                        f"{shape.num_layers} layers, hidden 2048, 16/8 heads, D 128, FFN 6144, vocab 3072, P=16, "
+                        f"{args.pool_tokens // 1024}k-token pool, GPU planner + fused sampler, CUDA graph",
+            "global_batch": BATCH * world,
+            "seq_len": CTX_HI,
+            "parallelism": f"dp{world} (request-sharded, no collective)",
+            "l2": "inputs larger than L2: ~7.8 GB of KV read per step",
+        },
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
+                "d2h_bytes_per_step": BATCH * 8},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "decode attention (decode_kernel + decode_merge_kernel)",
+                     "bytes_per_launch": attn_bytes, "us_per_launch": attn_ms * 1e3,
+                     "peak_source": f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds, shape.num_layers)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del ag, step
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

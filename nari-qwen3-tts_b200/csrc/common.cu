@@ -1,0 +1,36 @@
+// Host-side helpers shared by every entry point: error text, launch checks,
+// SM count, ABI version.
+#include <stdio.h>
+
+#include "common.cuh"
+
+namespace nqt {
+
+static thread_local char g_last_error[256] = "";
+
+void set_last_error(const char* what, cudaError_t err) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s", what, cudaGetErrorString(err));
+}
+
+int check_launch(const char* what) {
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    set_last_error(what, err);
+    return NQT_ERR_CUDA;
+  }
+  return NQT_OK;
+}
+
+int num_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return 148;
+  return sms;
+}
+
+}  // namespace nqt
+
+extern "C" int nqt_abi_version(void) { return 1; }
+
+extern "C" const char* nqt_last_error(void) { return nqt::g_last_error; }

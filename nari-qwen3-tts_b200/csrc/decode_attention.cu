@@ -1,0 +1,587 @@
+// Paged GQA decode attention for sm_100a: balanced split-KV, TMA page
+// gathers, online softmax, LSE merge.
+//
+// Work split.  For one KV-head group the batch's KV is a flat list of
+// 16-token tiles (sequence-major).  nqt_decode_plan writes the per-sequence
+// tile prefix sum on the device.  The decode launch has N persistent CTAs
+// per head group; CTA c streams tiles [T*c/N, T*(c+1)/N), crossing
+// sequence boundaries, so every CTA moves the same number of bytes whatever
+// the ragged lengths are.  A sequence covered by one CTA is written
+// straight to `out`; otherwise each covering CTA leaves a normalised
+// partial (O, lse) in slot 2c (its first segment) or 2c+1 (its last) and
+// the merge kernel combines them.  No CTA waits on another.
+//
+// Data path.  The layer view [pages, 2, P, Hkv, D] is described by a 4-D
+// tensor map {D, Hkv, P, pages*2}.  One TMA box {64, 1, 16, 2} brings
+// K and V of 16 tokens x 64 dims of one KV head (4 KB) into shared memory
+// with the 128-byte swizzle, so the ldmatrix reads of a head's 16 token
+// rows are bank-conflict free.  A producer warp keeps STAGES tiles in
+// flight through full/empty mbarriers; each consumer warp owns one KV head
+// and computes S^T = K Q^T and O^T += V^T P^T with m16n8k16 tensor-core
+// tiles (the GQA group's query heads are the N columns), keeping m, l and
+// O in registers.
+//
+// Reference: BatchDecodeWithPagedKVCacheWrapper.plan/run as bound at
+// executor/talker_kv.py:229-306 (FlashInfer 0.6.16): out[b, h] =
+// softmax(q[b,h] . K[b, :, h/G]^T * sm_scale) V[b, :, h/G] over the
+// (n_pages - 1) * P + last_page_len tokens of row b.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace nqt {
+namespace {
+
+constexpr int kTok = 16;           // tokens per TMA tile
+constexpr int kBoxBytes = 4096;    // [kind 2][tok 16][64 dims] bf16
+constexpr int kMaxSplitCtas = 640; // per head group
+constexpr int kHeaderBytes = 256;
+
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct WsLayout {
+  size_t tile_indptr;  // i32 [batch_cap + 1]
+  size_t part_lse;     // f32 [2 * kMaxSplitCtas * hq]
+  size_t part_o;       // f32 [2 * kMaxSplitCtas * hq * D]
+  size_t total;
+};
+
+WsLayout ws_layout(int batch_cap, int hq, int d) {
+  WsLayout w;
+  w.tile_indptr = kHeaderBytes;
+  w.part_lse = align_up(w.tile_indptr + 4 * static_cast<size_t>(batch_cap + 1), 256);
+  w.part_o = align_up(w.part_lse + 4 * static_cast<size_t>(2 * kMaxSplitCtas) * hq, 256);
+  w.total = align_up(w.part_o + 4 * static_cast<size_t>(2 * kMaxSplitCtas) * hq * d, 256);
+  return w;
+}
+
+struct DecodeArgs {
+  const __nv_bfloat16* q;
+  int64_t q_st, q_sh;
+  __nv_bfloat16* out;
+  int64_t o_st, o_sh;
+  const int32_t* indptr;
+  const int32_t* indices;
+  const int32_t* last_len;
+  const int32_t* tile_indptr;  // workspace
+  const int32_t* header;       // workspace: [0] = total tiles
+  float* part_lse;
+  float* part_o;
+  int32_t* status;
+  int batch, hq, hkv, group, page_size, total_pages, n_ctas;
+  float scale_log2;
+};
+
+// ------------------------------------------------------------------ plan
+// Single CTA: tiles_b = (n_pages_b - 1) * P/16 + ceil(last_len_b / 16),
+// exclusive prefix sum into tile_indptr, total into header[0].
+__global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* indptr, const int32_t* last_len,
+                                                           int batch, int page_size, int32_t* header,
+                                                           int32_t* tile_indptr) {
+  __shared__ int32_t warp_tot[32];
+  __shared__ int32_t carry_s;
+  const int tpp = page_size / kTok;
+  if (threadIdx.x == 0) carry_s = 0;
+  __syncthreads();
+  for (int start = 0; start < batch; start += blockDim.x) {
+    const int b = start + threadIdx.x;
+    int tiles = 0;
+    if (b < batch) {
+      const int n = indptr[b + 1] - indptr[b];
+      if (n > 0) {
+        int ll = last_len[b];
+        ll = ll < 1 ? 1 : (ll > page_size ? page_size : ll);
+        tiles = (n - 1) * tpp + (ll + kTok - 1) / kTok;
+      }
+    }
+    // block exclusive scan
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = tiles;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const int nw = blockDim.x >> 5;
+      int v = lane < nw ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFull, v, o);
+        if (lane >= o) v += y;
+      }
+      if (lane < nw) warp_tot[lane] = v;  // inclusive over warps
+    }
+    __syncthreads();
+    const int carry = carry_s;
+    const int excl = carry + (warp > 0 ? warp_tot[warp - 1] : 0) + incl - tiles;
+    if (b < batch) tile_indptr[b] = excl;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry_s = excl + tiles;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    tile_indptr[batch] = carry_s;
+    header[0] = carry_s;
+  }
+}
+
+// ------------------------------------------------------------------ decode
+__device__ __forceinline__ int64_t range_start(int64_t total, int c, int n) { return total * c / n; }
+
+// Sequence that owns flat tile t: last b with tile_indptr[b] <= t.
+__device__ __forceinline__ int find_seq(const int32_t* tile_indptr, int batch, int64_t t) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tile_indptr[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int D, int HPC, int STAGES>
+struct DecodeCfg {
+  static constexpr int kHalves = D / 64;
+  static constexpr int kStageBytes = HPC * kHalves * kBoxBytes;
+  static constexpr int kThreads = (HPC + 1) * 32;
+  static constexpr int kSmem = STAGES * kStageBytes + 1024 + 2 * STAGES * 8;
+};
+
+template <int D, int HPC, int STAGES>
+__global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                                DecodeArgs p) {
+  using Cfg = DecodeCfg<D, HPC, STAGES>;
+  constexpr int kHalves = Cfg::kHalves;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::kStageBytes);
+  uint64_t* empty = full + STAGES;
+
+  const int c = blockIdx.x;
+  const int kv0 = blockIdx.y * HPC;
+  const int64_t total = p.header[0];
+  const int64_t t_begin = range_start(total, c, p.n_ctas);
+  const int64_t t_end = range_start(total, c + 1, p.n_ctas);
+  if (t_begin >= t_end) return;  // uniform over the block
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tpp = p.page_size / kTok;
+  const int n_tiles = static_cast<int>(t_end - t_begin);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], HPC);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == HPC) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      prefetch_tensormap(&tmap);
+      int seq = find_seq(p.tile_indptr, p.batch, t_begin);
+      int seq_t0 = p.tile_indptr[seq];
+      int seq_t1 = p.tile_indptr[seq + 1];
+      for (int i = 0; i < n_tiles; ++i) {
+        const int64_t t = t_begin + i;
+        while (t >= seq_t1) {  // advance to the owning sequence (skips empty rows)
+          ++seq;
+          seq_t0 = seq_t1;
+          seq_t1 = p.tile_indptr[seq + 1];
+        }
+        const int s = i % STAGES;
+        if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, p.status)) break;
+        const int in_seq = static_cast<int>(t - seq_t0);
+        const int page_local = in_seq / tpp;
+        const int tile_in_page = in_seq - page_local * tpp;
+        int page = p.indices[p.indptr[seq] + page_local];
+        if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.total_pages)) {
+          report(p.status, NQT_DEV_BAD_PAGE);
+          page = p.total_pages;  // a box entirely outside the map: TMA fills zeros
+        }
+        mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+        uint8_t* dst = smem + s * Cfg::kStageBytes;
+#pragma unroll
+        for (int h = 0; h < HPC; ++h)
+#pragma unroll
+          for (int half = 0; half < kHalves; ++half)
+            tma_load_4d(dst + (h * kHalves + half) * kBoxBytes, &tmap, &full[s], half * 64, kv0 + h,
+                        tile_in_page * kTok, page * 2);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int kvh = kv0 + warp;
+  const int g = lane >> 2;
+  const int t4 = lane & 3;
+  const int group = p.group;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+
+  uint32_t qf[D / 16][2];
+  float o[D / 16][4];
+  float m0 = NEG_INF, m1 = NEG_INF, l0 = 0.f, l1 = 0.f;
+
+  int seq = find_seq(p.tile_indptr, p.batch, t_begin);
+  int seq_t0 = p.tile_indptr[seq];
+  int seq_t1 = p.tile_indptr[seq + 1];
+  bool seg_open = false;
+
+  // ldmatrix lane roles
+  const int lm_j = lane >> 3;
+  const int lm_r = lane & 7;
+
+  for (int i = 0; i < n_tiles; ++i) {
+    const int64_t t = t_begin + i;
+    while (t >= seq_t1) {
+      ++seq;
+      seq_t0 = seq_t1;
+      seq_t1 = p.tile_indptr[seq + 1];
+    }
+    if (!seg_open) {
+      // new segment: load this sequence's query heads of the group as B fragments
+      const int qhead = kvh * group + g;
+      const __nv_bfloat16* qrow = p.q + seq * p.q_st + static_cast<int64_t>(qhead) * p.q_sh;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        if (g < group) {
+          qf[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4);
+          qf[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4 + 8);
+        } else {
+          qf[kk][0] = 0u;
+          qf[kk][1] = 0u;
+        }
+      }
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      m0 = m1 = NEG_INF;
+      l0 = l1 = 0.f;
+      seg_open = true;
+    }
+    const bool last_tile_of_seq = (t == seq_t1 - 1);
+    int valid = kTok;
+    if (last_tile_of_seq) {
+      int ll = p.last_len[seq];
+      ll = ll < 1 ? 1 : (ll > p.page_size ? p.page_size : ll);
+      valid = ll - ((ll - 1) / kTok) * kTok;
+    }
+
+    const int s = i % STAGES;
+    if (!mbar_wait(&full[s], (i / STAGES) & 1, p.status)) return;
+    uint8_t* head_box = smem + s * Cfg::kStageBytes + warp * kHalves * kBoxBytes;
+
+    if (valid < kTok) {
+      // zero the V rows past the sequence end so 0 * stale never meets a NaN
+      const int rows = kTok - valid;
+      for (int idx = lane; idx < rows * 8 * kHalves; idx += 32) {
+        const int half = idx / (rows * 8);
+        const int rem = idx - half * rows * 8;
+        const int row = valid + rem / 8;
+        const int chunk = rem & 7;
+        *reinterpret_cast<uint4*>(head_box + half * kBoxBytes + 2048 + row * 128 + chunk * 16) =
+            make_uint4(0u, 0u, 0u, 0u);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+    }
+
+    // S^T[tok][n] = sum_d K[tok][d] Q[n][d]
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int half = kk >> 2;
+      const int chunk = ((kk & 3) << 1) + (lm_j >> 1);
+      const int tok = ((lm_j & 1) << 3) + lm_r;
+      const uint32_t addr = smem_addr(head_box + half * kBoxBytes) + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+      uint32_t a0, a1, a2, a3;
+      ldmatrix_x4(a0, a1, a2, a3, addr);
+      mma_bf16_16816(sc, a0, a1, a2, a3, qf[kk][0], qf[kk][1]);
+    }
+
+    // online softmax (log2 domain); lane holds heads 2*t4 (c0,c2) and 2*t4+1 (c1,c3)
+    const bool lo_ok = g < valid;
+    const bool hi_ok = g + 8 < valid;
+    const float s0 = lo_ok ? sc[0] * p.scale_log2 : NEG_INF;
+    const float s1 = lo_ok ? sc[1] * p.scale_log2 : NEG_INF;
+    const float s2 = hi_ok ? sc[2] * p.scale_log2 : NEG_INF;
+    const float s3 = hi_ok ? sc[3] * p.scale_log2 : NEG_INF;
+    float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(kFull, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(kFull, mx1, off));
+    }
+    const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+    const float al0 = exp2f(m0 - nm0), al1 = exp2f(m1 - nm1);
+    const float p0 = exp2f(s0 - nm0), p1 = exp2f(s1 - nm1);
+    const float p2 = exp2f(s2 - nm0), p3 = exp2f(s3 - nm1);
+    l0 = l0 * al0 + p0 + p2;
+    l1 = l1 * al1 + p1 + p3;
+    m0 = nm0;
+    m1 = nm1;
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      o[mt][0] *= al0;
+      o[mt][1] *= al1;
+      o[mt][2] *= al0;
+      o[mt][3] *= al1;
+    }
+
+    // P^T as the B operand: lane (g, t4) needs P[head g][tok 2t4, 2t4+1, 2t4+8, 2t4+9]
+    const uint32_t pack_a = pack_bf16x2(p0, p2);  // head 2*t4: tok g (lo), tok g+8 (hi)
+    const uint32_t pack_b = pack_bf16x2(p1, p3);  // head 2*t4+1
+    const int src1 = (2 * t4) * 4 + (g >> 1);
+    const int src2 = (2 * t4 + 1) * 4 + (g >> 1);
+    const uint32_t x1a = __shfl_sync(kFull, pack_a, src1);
+    const uint32_t x1b = __shfl_sync(kFull, pack_b, src1);
+    const uint32_t x2a = __shfl_sync(kFull, pack_a, src2);
+    const uint32_t x2b = __shfl_sync(kFull, pack_b, src2);
+    const uint32_t x1 = (g & 1) ? x1b : x1a;
+    const uint32_t x2 = (g & 1) ? x2b : x2a;
+    uint32_t pb0 = __byte_perm(x1, x2, 0x5410);
+    uint32_t pb1 = __byte_perm(x1, x2, 0x7632);
+    if (g >= group) pb0 = pb1 = 0u;
+
+    // O^T[d][n] += sum_tok V[tok][d] P[n][tok]
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      const int half = mt >> 2;
+      const int chunk = ((mt & 3) << 1) + (lm_j & 1);
+      const int tok = ((lm_j >> 1) << 3) + lm_r;
+      const uint32_t addr =
+          smem_addr(head_box + half * kBoxBytes + 2048) + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+      uint32_t a0, a1, a2, a3;
+      ldmatrix_x4_trans(a0, a1, a2, a3, addr);
+      mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    const bool seg_end = last_tile_of_seq || (i == n_tiles - 1);
+    if (seg_end) {
+      float lt0 = l0, lt1 = l1;
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        lt0 += __shfl_xor_sync(kFull, lt0, off);
+        lt1 += __shfl_xor_sync(kFull, lt1, off);
+      }
+      const float inv0 = 1.f / lt0, inv1 = 1.f / lt1;
+      const int ha = kvh * group + 2 * t4;  // query head of columns c0/c2
+      const bool whole = (t_begin <= seq_t0) && (t_end >= seq_t1);
+      if (whole) {
+        __nv_bfloat16* ob = p.out + seq * p.o_st;
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) {
+          const int d0 = mt * 16 + g;
+          if (2 * t4 < group) {
+            ob[ha * p.o_sh + d0] = __float2bfloat16_rn(o[mt][0] * inv0);
+            ob[ha * p.o_sh + d0 + 8] = __float2bfloat16_rn(o[mt][2] * inv0);
+          }
+          if (2 * t4 + 1 < group) {
+            ob[(ha + 1) * p.o_sh + d0] = __float2bfloat16_rn(o[mt][1] * inv1);
+            ob[(ha + 1) * p.o_sh + d0 + 8] = __float2bfloat16_rn(o[mt][3] * inv1);
+          }
+        }
+      } else {
+        const int slot = (t_begin >= seq_t0) ? 2 * c : 2 * c + 1;
+        float* po = p.part_o + static_cast<int64_t>(slot) * p.hq * D;
+        float* pl = p.part_lse + static_cast<int64_t>(slot) * p.hq;
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) {
+          const int d0 = mt * 16 + g;
+          if (2 * t4 < group) {
+            po[ha * D + d0] = o[mt][0] * inv0;
+            po[ha * D + d0 + 8] = o[mt][2] * inv0;
+          }
+          if (2 * t4 + 1 < group) {
+            po[(ha + 1) * D + d0] = o[mt][1] * inv1;
+            po[(ha + 1) * D + d0 + 8] = o[mt][3] * inv1;
+          }
+        }
+        if (g == 0) {
+          if (2 * t4 < group) pl[ha] = m0 + log2f(lt0);
+          if (2 * t4 + 1 < group) pl[ha + 1] = m1 + log2f(lt1);
+        }
+      }
+      seg_open = false;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ merge
+template <int D>
+__global__ void __launch_bounds__(D) decode_merge_kernel(DecodeArgs p) {
+  const int seq = blockIdx.x;
+  const int head = blockIdx.y;
+  const int d = threadIdx.x;
+  const int64_t total = p.header[0];
+  const int n = p.n_ctas;
+  const int64_t tb0 = p.tile_indptr[seq];
+  const int64_t tb1 = p.tile_indptr[seq + 1];
+  __nv_bfloat16* ob = p.out + seq * p.o_st + static_cast<int64_t>(head) * p.o_sh;
+  if (tb1 <= tb0) {
+    ob[d] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  // CTA owning tile t: max c with floor(total*c/n) <= t
+  const int c0 = static_cast<int>(((tb0 + 1) * n + total - 1) / total) - 1;
+  const int c1 = static_cast<int>((tb1 * n + total - 1) / total) - 1;
+  if (c0 == c1) return;  // written directly by the decode kernel
+  float mx = -__int_as_float(0x7f800000);
+  for (int c = c0; c <= c1; ++c) {
+    const int64_t st = range_start(total, c, n);
+    if (st == range_start(total, c + 1, n)) continue;  // a CTA with no tiles left no partial
+    const int slot = (st >= tb0) ? 2 * c : 2 * c + 1;
+    mx = fmaxf(mx, p.part_lse[static_cast<int64_t>(slot) * p.hq + head]);
+  }
+  float wsum = 0.f, acc = 0.f;
+  for (int c = c0; c <= c1; ++c) {
+    const int64_t st = range_start(total, c, n);
+    if (st == range_start(total, c + 1, n)) continue;
+    const int slot = (st >= tb0) ? 2 * c : 2 * c + 1;
+    const float w = exp2f(p.part_lse[static_cast<int64_t>(slot) * p.hq + head] - mx);
+    wsum += w;
+    acc += w * p.part_o[(static_cast<int64_t>(slot) * p.hq + head) * D + d];
+  }
+  ob[d] = __float2bfloat16_rn(acc / wsum);
+}
+
+// ------------------------------------------------------------------ host
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int encode_layer_map(CUtensorMap* map, const void* layer, int total_pages, int page_size, int hkv, int d) {
+  auto encode = get_encode();
+  if (encode == nullptr) return NQT_ERR_CUDA;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(hkv),
+                        static_cast<cuuint64_t>(page_size), static_cast<cuuint64_t>(total_pages) * 2};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(d) * 2, static_cast<cuuint64_t>(hkv) * d * 2,
+                           static_cast<cuuint64_t>(page_size) * hkv * d * 2};
+  cuuint32_t box[4] = {64, 1, kTok, 2};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(layer), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NQT_OK : NQT_ERR_CUDA;
+}
+
+template <int D, int HPC, int STAGES>
+int launch_decode(const CUtensorMap& map, DecodeArgs a, int groups, cudaStream_t s) {
+  using Cfg = DecodeCfg<D, HPC, STAGES>;
+  static int occ = -1;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(decode_kernel<D, HPC, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    int o = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, decode_kernel<D, HPC, STAGES>, Cfg::kThreads, Cfg::kSmem);
+    occ = o > 0 ? o : 1;
+  });
+  int n = num_sms() * occ / groups;
+  if (n < 1) n = 1;
+  if (n > kMaxSplitCtas) n = kMaxSplitCtas;
+  a.n_ctas = n;
+  decode_kernel<D, HPC, STAGES><<<dim3(n, groups), Cfg::kThreads, Cfg::kSmem, s>>>(map, a);
+  int rc = check_launch("decode_attention");
+  if (rc != NQT_OK) return rc;
+  decode_merge_kernel<D><<<dim3(a.batch, a.hq, 1), D, 0, s>>>(a);
+  return check_launch("decode_merge");
+}
+
+template <int D>
+int dispatch_hpc(const CUtensorMap& map, const DecodeArgs& a, cudaStream_t s) {
+  if (a.hkv % 4 == 0) return launch_decode<D, 4, 3>(map, a, a.hkv / 4, s);
+  if (a.hkv % 2 == 0) return launch_decode<D, 2, 4>(map, a, a.hkv / 2, s);
+  return launch_decode<D, 1, 4>(map, a, a.hkv, s);
+}
+
+}  // namespace
+}  // namespace nqt
+
+using namespace nqt;
+
+extern "C" size_t nqt_decode_workspace_bytes(int batch_capacity, int num_qo_heads, int head_dim) {
+  if (batch_capacity < 1 || num_qo_heads < 1 || head_dim < 1) return 0;
+  return ws_layout(batch_capacity, num_qo_heads, head_dim).total;
+}
+
+extern "C" int nqt_decode_plan(const int32_t* kv_indptr, const int32_t* last_page_len, int batch,
+                               int batch_capacity, int page_size, int num_qo_heads, int head_dim, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (!kv_indptr || !last_page_len || !workspace) return NQT_ERR_ARG;
+  if (batch < 1 || batch > batch_capacity || page_size < kTok || page_size % kTok) return NQT_ERR_ARG;
+  const WsLayout w = ws_layout(batch_capacity, num_qo_heads, head_dim);
+  if (workspace_bytes < w.total) return NQT_ERR_CAPACITY;
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  decode_plan_kernel<<<1, 1024, 0, as_stream(stream)>>>(kv_indptr, last_page_len, batch, page_size,
+                                                         reinterpret_cast<int32_t*>(base),
+                                                         reinterpret_cast<int32_t*>(base + w.tile_indptr));
+  return check_launch("decode_plan");
+}
+
+extern "C" int nqt_decode_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                                    const void* layer_cache, int total_pages, int page_size,
+                                    const int32_t* kv_indptr, const int32_t* kv_indices,
+                                    const int32_t* last_page_len, int batch, int batch_capacity, int num_qo_heads,
+                                    int num_kv_heads, int head_dim, float sm_scale, void* out,
+                                    int64_t out_stride_tok, int64_t out_stride_head, void* workspace,
+                                    size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!q || !layer_cache || !kv_indptr || !kv_indices || !last_page_len || !out || !workspace) return NQT_ERR_ARG;
+  if (batch < 1 || batch > batch_capacity || total_pages < 1) return NQT_ERR_ARG;
+  if (num_kv_heads < 1 || num_qo_heads % num_kv_heads) return NQT_ERR_ARG;
+  const int group = num_qo_heads / num_kv_heads;
+  if (group > 8 || num_kv_heads > 256) return NQT_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return NQT_ERR_UNSUPPORTED;
+  if (page_size < kTok || page_size % kTok || page_size > 256) return NQT_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(layer_cache) & 15) || (reinterpret_cast<uintptr_t>(q) & 3)) return NQT_ERR_ARG;
+  if ((q_stride_tok & 1) || (q_stride_head & 1)) return NQT_ERR_ARG;
+  if (static_cast<int64_t>(total_pages) * 2 >= (int64_t(1) << 31)) return NQT_ERR_UNSUPPORTED;
+  const WsLayout w = ws_layout(batch_capacity, num_qo_heads, head_dim);
+  if (workspace_bytes < w.total) return NQT_ERR_CAPACITY;
+  CUtensorMap map;
+  int rc = encode_layer_map(&map, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
+  if (rc != NQT_OK) return rc;
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  DecodeArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_st = q_stride_tok;
+  a.q_sh = q_stride_head;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.o_st = out_stride_tok;
+  a.o_sh = out_stride_head;
+  a.indptr = kv_indptr;
+  a.indices = kv_indices;
+  a.last_len = last_page_len;
+  a.tile_indptr = reinterpret_cast<const int32_t*>(base + w.tile_indptr);
+  a.header = reinterpret_cast<const int32_t*>(base);
+  a.part_lse = reinterpret_cast<float*>(base + w.part_lse);
+  a.part_o = reinterpret_cast<float*>(base + w.part_o);
+  a.status = status;
+  a.batch = batch;
+  a.hq = num_qo_heads;
+  a.hkv = num_kv_heads;
+  a.group = group;
+  a.page_size = page_size;
+  a.total_pages = total_pages;
+  a.n_ctas = 1;
+  a.scale_log2 = sm_scale * 1.4426950408889634f;
+  cudaStream_t s = as_stream(stream);
+  return head_dim == 128 ? dispatch_hpc<128>(map, a, s) : dispatch_hpc<64>(map, a, s);
+}

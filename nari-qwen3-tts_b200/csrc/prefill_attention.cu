@@ -1,0 +1,405 @@
+// Ragged causal prefill attention over paged KV (sm_100a).
+//
+// CTA = (64 query rows, one KV head).  A query row is a (token, head of the
+// GQA group) pair, so one K/V tile feeds every query head that reads it.
+// Rows of sequence b are the last qo_len_b positions of its KV: query token
+// i sees KV positions <= kv_len_b - qo_len_b + i.
+//
+// A producer warp streams K/V of 64-token blocks into shared memory with the
+// same 4-D tensor map as the decode kernel (one {64 dims, 1 head, 16 tokens,
+// K+V} box per page tile, 128-byte swizzle); four consumer warps own 16 rows
+// each and run S = Q K^T and O += P V with m16n8k16 tiles, fp32 online
+// softmax in registers.
+//
+// Reference: BatchPrefillWithPagedKVCacheWrapper.plan/run with causal=True
+// as bound at executor/talker_kv.py:140-226.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace nqt {
+namespace {
+
+constexpr int kTok = 16;
+constexpr int kBoxBytes = 4096;
+constexpr int kRows = 64;        // query rows per CTA
+constexpr int kBlockTok = 64;    // KV tokens per pipeline stage
+constexpr int kSub = kBlockTok / kTok;
+constexpr int kConsumers = 4;
+
+struct PrefillArgs {
+  const __nv_bfloat16* q;
+  int64_t q_st, q_sh;
+  __nv_bfloat16* out;
+  int64_t o_st, o_sh;
+  const int32_t* qo_indptr;
+  const int32_t* kv_indptr;
+  const int32_t* indices;
+  const int32_t* last_len;
+  int32_t* status;
+  int batch, hq, hkv, group, page_size, total_pages;
+  float scale_log2;
+};
+
+template <int D, int STAGES>
+struct PrefillCfg {
+  static constexpr int kHalves = D / 64;
+  static constexpr int kStageBytes = kSub * kHalves * kBoxBytes;  // K+V of 64 tokens, one head
+  static constexpr int kThreads = (kConsumers + 1) * 32;
+  static constexpr int kSmem = STAGES * kStageBytes + 1024 + 2 * STAGES * 8 + 64;
+};
+
+__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory"); }
+
+template <int D, int STAGES>
+__global__ void __launch_bounds__((kConsumers + 1) * 32) prefill_kernel(const __grid_constant__ CUtensorMap tmap,
+                                                                        PrefillArgs p) {
+  using Cfg = PrefillCfg<D, STAGES>;
+  constexpr int kHalves = Cfg::kHalves;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::kStageBytes);
+  uint64_t* empty = full + STAGES;
+  int* s_info = reinterpret_cast<int*>(empty + STAGES);
+
+  const int kvh = blockIdx.y;
+  const int G = p.group;
+  const int tokens_per_tile = kRows / G;
+  if (threadIdx.x == 0) {
+    // locate (sequence, tile) of this CTA
+    int remaining = blockIdx.x, seq = -1, tile = 0;
+    for (int b = 0; b < p.batch; ++b) {
+      const int qo = p.qo_indptr[b + 1] - p.qo_indptr[b];
+      const int tiles = qo > 0 ? (qo + tokens_per_tile - 1) / tokens_per_tile : 0;
+      if (remaining < tiles) {
+        seq = b;
+        tile = remaining;
+        break;
+      }
+      remaining -= tiles;
+    }
+    s_info[0] = seq;
+    s_info[1] = tile;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int seq = s_info[0];
+  if (seq < 0) return;
+  const int tile = s_info[1];
+  const int q0 = p.qo_indptr[seq];
+  const int qo_len = p.qo_indptr[seq + 1] - q0;
+  const int n_pages = p.kv_indptr[seq + 1] - p.kv_indptr[seq];
+  int ll = p.last_len[seq];
+  ll = ll < 1 ? 1 : (ll > p.page_size ? p.page_size : ll);
+  const int kv_len = n_pages > 0 ? (n_pages - 1) * p.page_size + ll : 0;
+  const int t_first = tile * tokens_per_tile;                       // first query token of the tile
+  const int t_last = min(qo_len, t_first + tokens_per_tile) - 1;    // last
+  const int shift = kv_len - qo_len;                                // query i sees keys <= shift + i
+  const int kv_hi = min(kv_len, shift + t_last + 1);
+  const int n_blocks = kv_hi > 0 ? (kv_hi + kBlockTok - 1) / kBlockTok : 0;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (warp == kConsumers) {
+    if (lane == 0 && n_blocks > 0) {
+      prefetch_tensormap(&tmap);
+      const int32_t* pages = p.indices + p.kv_indptr[seq];
+      for (int j = 0; j < n_blocks; ++j) {
+        const int s = j % STAGES;
+        if (j >= STAGES && !mbar_wait(&empty[s], ((j / STAGES) - 1) & 1, p.status)) break;
+        mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+        uint8_t* dst = smem + s * Cfg::kStageBytes;
+#pragma unroll
+        for (int st = 0; st < kSub; ++st) {
+          const int pos = j * kBlockTok + st * kTok;
+          const int pi = pos / p.page_size;
+          int page = p.total_pages;  // past the sequence: zero-filled box
+          if (pi < n_pages) {
+            page = pages[pi];
+            if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.total_pages)) {
+              report(p.status, NQT_DEV_BAD_PAGE);
+              page = p.total_pages;
+            }
+          }
+          const int tok_in_page = pos - pi * p.page_size;
+#pragma unroll
+          for (int half = 0; half < kHalves; ++half)
+            tma_load_4d(dst + (st * kHalves + half) * kBoxBytes, &tmap, &full[s], half * 64, kvh, tok_in_page,
+                        page * 2);
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int g = lane >> 2, t4 = lane & 3;
+  const int row0 = warp * 16 + g;  // rows of this lane: row0 and row0 + 8
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  int qtok[2], qhead[2];
+  bool qvalid[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = row0 + 8 * h;
+    qtok[h] = t_first + r / G;
+    qhead[h] = kvh * G + r % G;
+    qvalid[h] = qtok[h] < qo_len;
+  }
+  uint32_t qa[D / 16][4];
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (qvalid[h]) {
+        const __nv_bfloat16* qr = p.q + static_cast<int64_t>(q0 + qtok[h]) * p.q_st + static_cast<int64_t>(qhead[h]) * p.q_sh;
+        qa[kk][h] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + 2 * t4);
+        qa[kk][2 + h] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + 8 + 2 * t4);
+      } else {
+        qa[kk][h] = 0u;
+        qa[kk][2 + h] = 0u;
+      }
+    }
+  }
+  float o[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m[2] = {NEG_INF, NEG_INF}, l[2] = {0.f, 0.f};
+  const int lim0 = shift + qtok[0];  // last visible key of each row
+  const int lim1 = shift + qtok[1];
+  const int lm_j = lane >> 3, lm_r = lane & 7;
+
+  for (int j = 0; j < n_blocks; ++j) {
+    const int s = j % STAGES;
+    if (!mbar_wait(&full[s], (j / STAGES) & 1, p.status)) return;
+    uint8_t* stage = smem + s * Cfg::kStageBytes;
+    const int base = j * kBlockTok;
+    if (base + kBlockTok > kv_len) {
+      // zero V rows at or past kv_len (stale page contents never meet p = 0)
+      consumer_bar();
+      const int first_bad = max(0, kv_len - base);
+      const int n_bad = kBlockTok - first_bad;
+      for (int idx = threadIdx.x; idx < n_bad * kHalves * 8; idx += kConsumers * 32) {
+        const int t = first_bad + idx / (kHalves * 8);
+        const int rem = idx % (kHalves * 8);
+        const int half = rem / 8, chunk = rem % 8;
+        const int st = t / kTok, tr = t % kTok;
+        *reinterpret_cast<uint4*>(stage + (st * kHalves + half) * kBoxBytes + 2048 + tr * 128 + chunk * 16) =
+            make_uint4(0u, 0u, 0u, 0u);
+      }
+      fence_proxy_async_smem();
+      consumer_bar();
+    }
+    // S = Q K^T: 8 n-tiles of 8 tokens
+    float sc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+    for (int st = 0; st < kSub; ++st) {
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int half = kk >> 2;
+        const int chunk = ((kk & 3) << 1) + (lm_j & 1);
+        const int tok = ((lm_j >> 1) << 3) + lm_r;
+        const uint32_t addr = smem_addr(stage + (st * kHalves + half) * kBoxBytes) + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(b0, b1, b2, b3, addr);
+        // b0,b1: tokens 0-7 (k lo, k hi); b2,b3: tokens 8-15
+        mma_bf16_16816(sc[2 * st], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+        mma_bf16_16816(sc[2 * st + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
+      }
+    }
+    // mask + online softmax; lane rows: g (c0,c1) and g+8 (c2,c3); cols 2*t4, 2*t4+1
+    float mx[2] = {NEG_INF, NEG_INF};
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int key = base + n * 8 + 2 * t4;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int kpos = key + (e & 1);
+        const int lim = (e < 2) ? lim0 : lim1;
+        const bool ok = (kpos <= lim) && (kpos < kv_len);
+        sc[n][e] = ok ? sc[n][e] * p.scale_log2 : NEG_INF;
+        mx[e >> 1] = fmaxf(mx[e >> 1], sc[n][e]);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(kFull, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(kFull, mx[h], 2));
+    }
+    float alpha[2], nm[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      nm[h] = fmaxf(m[h], mx[h]);
+      // rows with nothing visible yet keep m = -inf; exp2(-inf - -inf) would be NaN
+      const float ref = nm[h] == NEG_INF ? 0.f : nm[h];
+      alpha[h] = exp2f(m[h] - ref);
+      m[h] = nm[h];
+      nm[h] = ref;
+    }
+    float rs[2] = {0.f, 0.f};
+    uint32_t pa[4][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float p0 = exp2f(sc[n][0] - nm[0]);
+      const float p1 = exp2f(sc[n][1] - nm[0]);
+      const float p2 = exp2f(sc[n][2] - nm[1]);
+      const float p3 = exp2f(sc[n][3] - nm[1]);
+      rs[0] += p0 + p1;
+      rs[1] += p2 + p3;
+      // A fragment of P for k-step n/2: a0/a1 from even n-tile, a2/a3 from odd
+      const int ks = n >> 1;
+      if ((n & 1) == 0) {
+        pa[ks][0] = pack_bf16x2(p0, p1);
+        pa[ks][1] = pack_bf16x2(p2, p3);
+      } else {
+        pa[ks][2] = pack_bf16x2(p0, p1);
+        pa[ks][3] = pack_bf16x2(p2, p3);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) l[h] = l[h] * alpha[h] + rs[h];
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      o[n][0] *= alpha[0];
+      o[n][1] *= alpha[0];
+      o[n][2] *= alpha[1];
+      o[n][3] *= alpha[1];
+    }
+    // O += P V: per k-step (16 tokens = one sub-tile), two d-chunks per ldmatrix.x4.trans
+#pragma unroll
+    for (int ks = 0; ks < kSub; ++ks) {
+#pragma unroll
+      for (int nc = 0; nc < D / 16; ++nc) {
+        const int half = nc >> 2;
+        const int chunk = ((nc & 3) << 1) + (lm_j >> 1);
+        const int tok = ((lm_j & 1) << 3) + lm_r;
+        const uint32_t addr =
+            smem_addr(stage + (ks * kHalves + half) * kBoxBytes + 2048) + tok * 128 + ((chunk ^ (tok & 7)) << 4);
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(b0, b1, b2, b3, addr);
+        // b0: (tok 0-7, chunk c) b1: (tok 8-15, chunk c) b2: (tok 0-7, c+1) b3: (tok 8-15, c+1)
+        mma_bf16_16816(o[2 * nc], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b0, b1);
+        mma_bf16_16816(o[2 * nc + 1], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // finalize
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l[h] += __shfl_xor_sync(kFull, l[h], 1);
+    l[h] += __shfl_xor_sync(kFull, l[h], 2);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (!qvalid[h]) continue;
+    const float inv = l[h] > 0.f ? 1.f / l[h] : 0.f;
+    __nv_bfloat16* orow = p.out + static_cast<int64_t>(q0 + qtok[h]) * p.o_st + static_cast<int64_t>(qhead[h]) * p.o_sh;
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n)
+      *reinterpret_cast<__nv_bfloat162*>(orow + n * 8 + 2 * t4) =
+          __floats2bfloat162_rn(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int encode_map(CUtensorMap* map, const void* layer, int total_pages, int page_size, int hkv, int d) {
+  auto encode = get_encode();
+  if (encode == nullptr) return NQT_ERR_CUDA;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(hkv),
+                        static_cast<cuuint64_t>(page_size), static_cast<cuuint64_t>(total_pages) * 2};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(d) * 2, static_cast<cuuint64_t>(hkv) * d * 2,
+                           static_cast<cuuint64_t>(page_size) * hkv * d * 2};
+  cuuint32_t box[4] = {64, 1, kTok, 2};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(layer), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NQT_OK : NQT_ERR_CUDA;
+}
+
+template <int D, int STAGES>
+int launch_prefill(const CUtensorMap& map, const PrefillArgs& a, int grid_x, cudaStream_t s) {
+  using Cfg = PrefillCfg<D, STAGES>;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(prefill_kernel<D, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+  });
+  prefill_kernel<D, STAGES><<<dim3(grid_x, a.hkv), Cfg::kThreads, Cfg::kSmem, s>>>(map, a);
+  return check_launch("prefill_attention");
+}
+
+}  // namespace
+}  // namespace nqt
+
+using namespace nqt;
+
+extern "C" int nqt_prefill_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                                     const void* layer_cache, int total_pages, int page_size,
+                                     const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_indices,
+                                     const int32_t* last_page_len, int batch, int total_q_tokens, int num_qo_heads,
+                                     int num_kv_heads, int head_dim, float sm_scale, void* out,
+                                     int64_t out_stride_tok, int64_t out_stride_head, int32_t* status,
+                                     void* stream) {
+  if (!q || !layer_cache || !qo_indptr || !kv_indptr || !kv_indices || !last_page_len || !out) return NQT_ERR_ARG;
+  if (batch < 1 || total_q_tokens < 0 || total_pages < 1) return NQT_ERR_ARG;
+  if (num_kv_heads < 1 || num_qo_heads % num_kv_heads) return NQT_ERR_ARG;
+  const int group = num_qo_heads / num_kv_heads;
+  if (group > 8 || (kRows % group)) return NQT_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return NQT_ERR_UNSUPPORTED;
+  if (page_size < kTok || page_size % kTok || page_size > 256) return NQT_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(layer_cache) & 15) || (reinterpret_cast<uintptr_t>(q) & 3) ||
+      (reinterpret_cast<uintptr_t>(out) & 3))
+    return NQT_ERR_ARG;
+  if ((q_stride_tok & 1) || (q_stride_head & 1) || (out_stride_tok & 1) || (out_stride_head & 1)) return NQT_ERR_ARG;
+  if (static_cast<int64_t>(total_pages) * 2 >= (int64_t(1) << 31)) return NQT_ERR_UNSUPPORTED;
+  if (total_q_tokens == 0) return NQT_OK;
+  CUtensorMap map;
+  int rc = encode_map(&map, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
+  if (rc != NQT_OK) return rc;
+  PrefillArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_st = q_stride_tok;
+  a.q_sh = q_stride_head;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.o_st = out_stride_tok;
+  a.o_sh = out_stride_head;
+  a.qo_indptr = qo_indptr;
+  a.kv_indptr = kv_indptr;
+  a.indices = kv_indices;
+  a.last_len = last_page_len;
+  a.status = status;
+  a.batch = batch;
+  a.hq = num_qo_heads;
+  a.hkv = num_kv_heads;
+  a.group = group;
+  a.page_size = page_size;
+  a.total_pages = total_pages;
+  a.scale_log2 = sm_scale * 1.4426950408889634f;
+  const int tokens_per_tile = kRows / group;
+  const int grid_x = (total_q_tokens + tokens_per_tile - 1) / tokens_per_tile + batch;
+  cudaStream_t s = as_stream(stream);
+  return head_dim == 128 ? launch_prefill<128, 3>(map, a, grid_x, s) : launch_prefill<64, 4>(map, a, grid_x, s);
+}

@@ -1,0 +1,337 @@
+"""Attention-math entry points with the reference's names and contracts.
+
+Each function validates its arguments the way the reference does
+(model/kernels.py) and raises the same exception types before any launch,
+then calls the sm_100a kernel through libnqt's C ABI on torch's current
+stream.  There is no CPU path: non-CUDA tensors are rejected.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import call, ptr
+
+
+def _status_for(device: torch.device) -> torch.Tensor:
+    return device_status(device)
+
+
+_STATUS: dict[int, torch.Tensor] = {}
+
+
+def device_status(device: torch.device) -> torch.Tensor:
+    """Per-device int32 status word that kernels OR error bits into."""
+
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    word = _STATUS.get(index)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+        _STATUS[index] = word
+    return word
+
+
+def read_status(device: torch.device) -> int:
+    """Host read of the status word (synchronises); 0 means no device error."""
+
+    return int(device_status(device).item())
+
+
+def clear_status(device: torch.device) -> None:
+    device_status(device).zero_()
+
+
+def paired_qk_norm_rope_paged_cache_(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    query_weight: torch.Tensor,
+    key_weight: torch.Tensor,
+    position_ids: torch.Tensor,
+    epsilon: float,
+    rope_theta: float,
+    layer_cache: torch.Tensor,
+    write_pages: torch.Tensor,
+    write_offsets: torch.Tensor,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Normalise/rotate QK in place and stage K/V into the paged cache.
+
+    Contract of model/kernels.py:94-160: per (token, head) fp32 RMSNorm,
+    times the weight, rounded to the element type, then RoPE; rotated K and
+    raw V land in layer_cache[write_pages[t], 0/1, write_offsets[t]].
+    """
+
+    if query.ndim != 3 or key.ndim != 3 or value.ndim != 3:
+        raise ValueError("Qwen3-TTS QKV tensors must have rank three")
+    tokens, query_heads, head_dim = query.shape
+    if key.shape != value.shape or key.shape[0] != tokens or key.shape[2] != head_dim:
+        raise ValueError("Qwen3-TTS QKV shapes are incompatible")
+    key_heads = key.shape[1]
+    if query.device.type != "cuda" or not (query.device == key.device == value.device == layer_cache.device):
+        raise ValueError("paired QKV paged staging requires one CUDA device")
+    if not (query.dtype == key.dtype == value.dtype == layer_cache.dtype):
+        raise TypeError("paired QKV paged staging requires one dtype")
+    if head_dim % 2 or query_weight.shape != (head_dim,) or key_weight.shape != (head_dim,):
+        raise ValueError("QK norm weights must match an even head dimension")
+    if position_ids.shape != (tokens,) or write_pages.shape != (tokens,) or write_offsets.shape != (tokens,):
+        raise ValueError("paged QKV metadata must contain one entry per token")
+    if layer_cache.ndim != 5 or layer_cache.shape[1] != 2 or layer_cache.shape[3:] != (key_heads, head_dim):
+        raise ValueError("paged QKV cache has an invalid layout")
+    if not all(tensor.stride(-1) == 1 for tensor in (query, key, value, layer_cache)):
+        raise ValueError("QKV and paged cache must be contiguous per head")
+    if not layer_cache.is_contiguous():
+        raise ValueError("paged QKV cache must be contiguous")
+    for t in (position_ids, write_pages, write_offsets):
+        if t.dtype != torch.long or not t.is_contiguous():
+            raise TypeError("paged QKV metadata must be contiguous int64")
+    if query_weight.dtype != query.dtype or key_weight.dtype != query.dtype:
+        query_weight = query_weight.to(query.dtype)
+        key_weight = key_weight.to(query.dtype)
+    if tokens == 0:
+        return query, key
+    device = query.device
+    call(
+        "nqt_qk_norm_rope_paged_kv_write",
+        ptr(query), query.stride(0), query.stride(1),
+        ptr(key), key.stride(0), key.stride(1),
+        ptr(value), value.stride(0), value.stride(1),
+        ptr(query_weight.contiguous()), ptr(key_weight.contiguous()),
+        ptr(position_ids), ptr(write_pages), ptr(write_offsets),
+        ptr(layer_cache), layer_cache.shape[0], layer_cache.shape[2],
+        tokens, query_heads, key_heads, head_dim,
+        float(epsilon), float(rope_theta), _lib.dtype_code(query.dtype),
+        ptr(device_status(device)), _lib.stream_handle(device),
+    )
+    return query, key
+
+
+def _validate_qk(query, key, query_weight, key_weight, positions):
+    if query.ndim != 3 or key.ndim != 3:
+        raise ValueError("QK tensors must have shape [tokens, heads, head_dim]")
+    tokens, query_heads, head_dim = query.shape
+    if key.shape[0] != tokens or key.shape[2] != head_dim or head_dim % 2:
+        raise ValueError("QK shapes are incompatible")
+    key_heads = key.shape[1]
+    if query.device.type != "cuda" or key.device != query.device or query.dtype != key.dtype:
+        raise ValueError("paired QK transform requires one CUDA dtype/device")
+    if query.stride(-1) != 1 or key.stride(-1) != 1:
+        raise ValueError("QK tensors must be contiguous per head")
+    if positions.shape != (tokens,) or positions.device != query.device:
+        raise ValueError("positions must contain one CUDA value per token")
+    if query_weight.shape != (head_dim,) or key_weight.shape != (head_dim,):
+        raise ValueError("QK norm weights must match head_dim")
+    return tokens, query_heads, key_heads, head_dim
+
+
+def paired_qk_norm_rope_(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    query_weight: torch.Tensor,
+    key_weight: torch.Tensor,
+    positions: torch.Tensor,
+    epsilon: float,
+    rope_theta: float,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """QK transform with the bf16 rounding boundary (model/kernels.py:275-332)."""
+
+    tokens, query_heads, key_heads, head_dim = _validate_qk(query, key, query_weight, key_weight, positions)
+    if tokens == 0:
+        return query, key
+    positions = positions.to(torch.long)
+    device = query.device
+    call(
+        "nqt_qk_norm_rope_dense",
+        ptr(query), query.stride(0), query.stride(1),
+        ptr(key), key.stride(0), key.stride(1),
+        None, 0, 0,
+        ptr(query_weight.to(query.dtype).contiguous()), ptr(key_weight.to(query.dtype).contiguous()),
+        ptr(positions), positions.stride(0),
+        None, None, 0, 0, 0, 0,
+        tokens, query_heads, key_heads, head_dim,
+        float(epsilon), float(rope_theta), 1, _lib.dtype_code(query.dtype),
+        ptr(device_status(device)), _lib.stream_handle(device),
+    )
+    return query, key
+
+
+def paired_qk_norm_rope_dense_cache_(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    query_weight: torch.Tensor,
+    key_weight: torch.Tensor,
+    positions: torch.Tensor,
+    epsilon: float,
+    rope_theta: float,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    cache_position: int,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """One-token QK transform plus dense CP cache write (model/kernels.py:335-405)."""
+
+    tokens, query_heads, key_heads, head_dim = _validate_qk(query, key, query_weight, key_weight, positions)
+    expected = (tokens, key_cache.shape[1], key_heads, head_dim)
+    if value.shape != (tokens, key_heads, head_dim) or key_cache.shape != expected or value_cache.shape != expected:
+        raise ValueError("dense CP QKV cache shape mismatch")
+    if not 0 <= cache_position < key_cache.shape[1]:
+        raise ValueError("dense CP cache position is invalid")
+    if not (value.device == key_cache.device == value_cache.device == query.device):
+        raise ValueError("dense CP QKV cache requires one CUDA device")
+    if not (value.dtype == key_cache.dtype == value_cache.dtype == query.dtype):
+        raise TypeError("dense CP QKV cache requires one dtype")
+    if key_cache.stride() != value_cache.stride() or key_cache.stride(-1) != 1 or value.stride(-1) != 1:
+        raise ValueError("dense CP caches must share a layout with unit head_dim stride")
+    if tokens == 0:
+        return query, key
+    positions = positions.to(torch.long)
+    device = query.device
+    call(
+        "nqt_qk_norm_rope_dense",
+        ptr(query), query.stride(0), query.stride(1),
+        ptr(key), key.stride(0), key.stride(1),
+        ptr(value), value.stride(0), value.stride(1),
+        ptr(query_weight.to(query.dtype).contiguous()), ptr(key_weight.to(query.dtype).contiguous()),
+        ptr(positions), positions.stride(0),
+        ptr(key_cache), ptr(value_cache), key_cache.stride(0), key_cache.stride(1), key_cache.stride(2),
+        int(cache_position),
+        tokens, query_heads, key_heads, head_dim,
+        float(epsilon), float(rope_theta), 0, _lib.dtype_code(query.dtype),
+        ptr(device_status(device)), _lib.stream_handle(device),
+    )
+    return query, key
+
+
+def decode_attn_nhd_short_cache(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    cache_length: int,
+) -> torch.Tensor:
+    """Short-cache one-query attention (model/kernels.py:466-520)."""
+
+    if not isinstance(cache_length, int) or isinstance(cache_length, bool) or not 1 <= cache_length <= 16:
+        raise ValueError("short-cache attention requires cache_length in [1, 16]")
+    squeeze = query.ndim == 4
+    if squeeze:
+        if query.shape[1] != 1:
+            raise ValueError("short-cache attention supports one query token")
+        query = query.squeeze(1)
+    if query.ndim != 3 or key_cache.ndim != 4 or key_cache.shape != value_cache.shape:
+        raise ValueError("short-cache QKV ranks are invalid")
+    rows, query_heads, head_dim = query.shape
+    cache_rows, capacity, key_heads, cache_head_dim = key_cache.shape
+    if (cache_rows, cache_head_dim) != (rows, head_dim) or cache_length > capacity:
+        raise ValueError("short-cache QKV shapes are incompatible")
+    if query_heads % key_heads or query.device.type != "cuda":
+        raise ValueError("short-cache attention requires compatible CUDA heads")
+    if key_cache.stride() != value_cache.stride() or key_cache.stride(-1) != 1 or query.stride(-1) != 1:
+        raise ValueError("short-cache tensors must be contiguous per head with one cache layout")
+    output = torch.empty((rows, query_heads, head_dim), dtype=query.dtype, device=query.device)
+    device = query.device
+    call(
+        "nqt_cp_short_attention",
+        ptr(query), query.stride(0), query.stride(1),
+        ptr(key_cache), ptr(value_cache), key_cache.stride(0), key_cache.stride(1), key_cache.stride(2),
+        cache_length, rows, query_heads, key_heads, head_dim, 1.0 / (head_dim**0.5),
+        ptr(output), output.stride(0), output.stride(1),
+        ptr(device_status(device)), _lib.stream_handle(device),
+    )
+    return output.unsqueeze(1) if squeeze else output
+
+
+def cp_decode_attention_(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    query_weight: torch.Tensor,
+    key_weight: torch.Tensor,
+    positions: torch.Tensor,
+    epsilon: float,
+    rope_theta: float,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    cache_position: int,
+) -> torch.Tensor:
+    """Fused code-predictor decode step: the dense-cache QK transform and
+    write of ``paired_qk_norm_rope_dense_cache_`` followed by
+    ``decode_attn_nhd_short_cache`` over ``cache_position + 1`` positions,
+    in one launch (model/components.py:309-345).  Returns [rows, Hq, D]."""
+
+    tokens, query_heads, key_heads, head_dim = _validate_qk(query, key, query_weight, key_weight, positions)
+    expected = (tokens, key_cache.shape[1], key_heads, head_dim)
+    if value.shape != (tokens, key_heads, head_dim) or key_cache.shape != expected or value_cache.shape != expected:
+        raise ValueError("dense CP QKV cache shape mismatch")
+    if not 0 <= cache_position < key_cache.shape[1]:
+        raise ValueError("dense CP cache position is invalid")
+    if not (value.dtype == key_cache.dtype == value_cache.dtype == query.dtype == torch.bfloat16):
+        raise TypeError("fused CP attention requires bf16 tensors")
+    if key_cache.stride() != value_cache.stride() or key_cache.stride(-1) != 1 or value.stride(-1) != 1:
+        raise ValueError("dense CP caches must share a layout with unit head_dim stride")
+    positions = positions.to(torch.long)
+    output = torch.empty((tokens, query_heads, head_dim), dtype=query.dtype, device=query.device)
+    device = query.device
+    call(
+        "nqt_cp_decode_attention",
+        ptr(query), query.stride(0), query.stride(1),
+        ptr(key), key.stride(0), key.stride(1),
+        ptr(value), value.stride(0), value.stride(1),
+        ptr(query_weight.to(query.dtype).contiguous()), ptr(key_weight.to(query.dtype).contiguous()),
+        ptr(positions), positions.stride(0),
+        ptr(key_cache), ptr(value_cache), key_cache.stride(0), key_cache.stride(1), key_cache.stride(2),
+        key_cache.shape[1], int(cache_position),
+        tokens, query_heads, key_heads, head_dim,
+        float(epsilon), float(rope_theta), 1.0 / (head_dim**0.5),
+        ptr(output), output.stride(0), output.stride(1),
+        ptr(device_status(device)), _lib.stream_handle(device),
+    )
+    return output
+
+
+__all__ = [
+    "clear_status",
+    "cp_decode_attention_",
+    "decode_attn_nhd_short_cache",
+    "device_status",
+    "paired_qk_norm_rope_",
+    "paired_qk_norm_rope_dense_cache_",
+    "paired_qk_norm_rope_paged_cache_",
+    "read_status",
+]
+
+
+# ---------------------------------------------------------------- layer glue
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm over the last dim (flashinfer.norm.rmsnorm at model/layers.py:80-100)."""
+
+    if x.stride(-1) != 1 or weight.dtype != x.dtype:
+        raise ValueError("rmsnorm needs rows contiguous in the hidden dim and a weight of the input dtype")
+    flat = x.reshape(-1, x.shape[-1])
+    if out is None:
+        out = torch.empty_like(flat)
+    call("nqt_rmsnorm", ptr(flat), flat.stride(0), ptr(weight), ptr(out), out.stride(0), flat.shape[0],
+         flat.shape[1], float(eps), _lib.dtype_code(x.dtype), _lib.stream_handle(x.device))
+    return out.view(x.shape)
+
+
+def fused_add_rmsnorm_(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float) -> None:
+    """In place: residual <- x + residual; x <- rmsnorm(residual) * weight
+    (flashinfer.norm.fused_add_rmsnorm at model/layers.py:42-77)."""
+
+    if not (x.is_contiguous() and residual.is_contiguous()) or x.shape != residual.shape:
+        raise ValueError("fused_add_rmsnorm needs contiguous tensors of one shape")
+    hidden = x.shape[-1]
+    call("nqt_fused_add_rmsnorm", ptr(x), ptr(residual), ptr(weight), x.numel() // hidden, hidden, float(eps),
+         _lib.dtype_code(x.dtype), _lib.stream_handle(x.device))
+
+
+def silu_and_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(gate) * up for gate_up = [gate | up] (model/layers.py:28-39)."""
+
+    d = gate_up.shape[-1] // 2
+    flat = gate_up.reshape(-1, 2 * d)
+    if out is None:
+        out = torch.empty((flat.shape[0], d), dtype=gate_up.dtype, device=gate_up.device)
+    call("nqt_silu_and_mul", ptr(flat), flat.stride(0), ptr(out), out.stride(0), flat.shape[0], d,
+         _lib.dtype_code(gate_up.dtype), _lib.stream_handle(gate_up.device))
+    return out.view(*gate_up.shape[:-1], d)

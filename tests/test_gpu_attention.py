@@ -1,0 +1,223 @@
+"""GPU parity: QK norm/RoPE + paged K/V write, paged decode, causal prefill and
+the code-predictor kernels against the CPU oracle (through the C ABI)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import attention as oatt
+from tests._paged import make_paged
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2  # bf16 attention outputs
+
+
+def _decode_case(nqt, cuda, lens, *, page_size=16, hq=16, hkv=8, d=128, seed=0, strided=False):
+    cache, indptr, indices, last = make_paged(lens, page_size=page_size, hkv=hkv, d=d, seed=seed)
+    g = torch.Generator().manual_seed(seed + 1)
+    rows = len(lens)
+    if strided:  # q as a view of a packed qkv projection, like layers.py:296-306
+        qkv = torch.randn(rows, hq * d + 2 * hkv * d, generator=g).to(torch.bfloat16)
+        q_cpu = qkv[:, : hq * d].view(rows, hq, d)
+        q_dev = qkv.to(cuda)[:, : hq * d].view(rows, hq, d)
+    else:
+        q_cpu = torch.randn(rows, hq, d, generator=g).to(torch.bfloat16)
+        q_dev = q_cpu.to(cuda)
+    ws = torch.zeros(nqt.lib().nqt_decode_workspace_bytes(rows, hq, d), dtype=torch.uint8, device=cuda)
+    out = nqt.batch_decode_paged(q_dev, cache.to(cuda), indptr.to(cuda), indices.to(cuda), last.to(cuda), ws)
+    torch.cuda.synchronize()
+    want = oatt.paged_decode(q_cpu.float(), cache.float(), indptr, indices, last)
+    return out.float().cpu(), want
+
+
+@pytest.mark.parametrize(
+    "lens",
+    [
+        [int(x) for x in torch.randint(16, 513, (8,), generator=torch.Generator().manual_seed(0))],  # config 1
+        [1, 15, 16, 17, 31, 32, 33],
+        [4096],
+        [1],
+        [2048, 1, 700, 64, 3, 1999],
+    ],
+)
+def test_decode_matches_oracle(nqt, cuda, lens):
+    got, want = _decode_case(nqt, cuda, lens)
+    assert torch.isfinite(got).all()
+    torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
+    assert nqt.kernels.read_status(cuda) == 0
+
+
+def test_decode_config2_shapes(nqt, cuda):
+    lens = torch.randint(64, 2049, (64,), generator=torch.Generator().manual_seed(2)).tolist()
+    got, want = _decode_case(nqt, cuda, lens, seed=2, strided=True)
+    torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
+
+
+@pytest.mark.parametrize("page_size", [32, 64, 128])
+def test_decode_page_sizes(nqt, cuda, page_size):
+    got, want = _decode_case(nqt, cuda, [5, 130, 333, 1024], page_size=page_size, seed=3)
+    torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
+
+
+@pytest.mark.parametrize(("hq", "hkv", "d"), [(16, 8, 64), (8, 8, 128), (16, 4, 128), (8, 2, 64), (6, 3, 128)])
+def test_decode_head_layouts(nqt, cuda, hq, hkv, d):
+    got, want = _decode_case(nqt, cuda, [77, 300, 16], hq=hq, hkv=hkv, d=d, seed=4)
+    torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
+
+
+def test_decode_golden_fixture(nqt, cuda, golden):
+    g = golden("attention.pt")["paged"]
+    cache = g["cache"].to(cuda)
+    rows = g["q_decode"].shape[0]
+    ws = torch.zeros(nqt.lib().nqt_decode_workspace_bytes(rows, 16, 128), dtype=torch.uint8, device=cuda)
+    out = nqt.batch_decode_paged(g["q_decode"].to(torch.bfloat16).to(cuda), cache, g["indptr"].to(cuda),
+                                 g["indices"].to(cuda), g["last_page_len"].to(cuda), ws)
+    torch.testing.assert_close(out.float().cpu(), g["decode_out"], atol=ATOL, rtol=0)
+
+
+def test_decode_bad_page_id_reports_status(nqt, cuda):
+    cache, indptr, indices, last = make_paged([40, 40], seed=5)
+    indices[1] = cache.shape[0] + 7  # outside the pool: read as zeros, flagged, no fault
+    nqt.kernels.clear_status(cuda)
+    ws = torch.zeros(nqt.lib().nqt_decode_workspace_bytes(2, 16, 128), dtype=torch.uint8, device=cuda)
+    q = torch.randn(2, 16, 128).to(torch.bfloat16)
+    out = nqt.batch_decode_paged(q.to(cuda), cache.to(cuda), indptr.to(cuda), indices.to(cuda), last.to(cuda), ws)
+    torch.cuda.synchronize()
+    assert nqt.kernels.read_status(cuda) & 0x1
+    assert torch.isfinite(out.float()).all()
+    nqt.kernels.clear_status(cuda)
+
+
+def _prefill_case(nqt, cuda, lens, qo_lens, *, page_size=16, hq=16, hkv=8, d=128, seed=0):
+    cache, indptr, indices, last = make_paged(lens, page_size=page_size, hkv=hkv, d=d, seed=seed)
+    qo_indptr = torch.tensor([0, *torch.tensor(qo_lens).cumsum(0).tolist()], dtype=torch.int32)
+    g = torch.Generator().manual_seed(seed + 1)
+    q = torch.randn(int(qo_indptr[-1]), hq, d, generator=g).to(torch.bfloat16)
+    out = nqt.batch_prefill_paged(q.to(cuda), cache.to(cuda), qo_indptr.to(cuda), indptr.to(cuda),
+                                  indices.to(cuda), last.to(cuda))
+    torch.cuda.synchronize()
+    want = oatt.paged_prefill(q.float(), cache.float(), qo_indptr, indptr, indices, last)
+    return out.float().cpu(), want
+
+
+@pytest.mark.parametrize(
+    ("lens", "qo_lens"),
+    [
+        ([37, 1, 300, 128], [37, 1, 45, 128]),
+        ([16, 17, 64, 65], [1, 17, 33, 2]),
+        ([1024, 700], [1024, 500]),
+        ([5, 200, 33], [0, 64, 33]),
+    ],
+)
+def test_prefill_matches_oracle(nqt, cuda, lens, qo_lens):
+    got, want = _prefill_case(nqt, cuda, lens, qo_lens)
+    assert torch.isfinite(got).all()
+    torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
+
+
+@pytest.mark.parametrize(("hq", "hkv", "d", "page_size"), [(16, 8, 64, 16), (8, 8, 128, 32), (16, 2, 128, 64)])
+def test_prefill_layouts(nqt, cuda, hq, hkv, d, page_size):
+    got, want = _prefill_case(nqt, cuda, [90, 260], [90, 31], hq=hq, hkv=hkv, d=d, page_size=page_size, seed=7)
+    torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
+
+
+def test_prefill_golden_fixture(nqt, cuda, golden):
+    g = golden("attention.pt")["paged"]
+    out = nqt.batch_prefill_paged(g["q_prefill"].to(torch.bfloat16).to(cuda), g["cache"].to(cuda),
+                                  g["qo_indptr"].to(cuda), g["indptr"].to(cuda), g["indices"].to(cuda),
+                                  g["last_page_len"].to(cuda))
+    torch.testing.assert_close(out.float().cpu(), g["prefill_out"], atol=ATOL, rtol=0)
+
+
+def _qk_inputs(tokens, hq, hkv, d, seed):
+    g = torch.Generator().manual_seed(seed)
+    qkv = torch.randn(tokens, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    return qkv, qw, kw
+
+
+def _split(qkv, hq, hkv, d):
+    t = qkv.shape[0]
+    return (qkv[:, : hq * d].view(t, hq, d), qkv[:, hq * d: (hq + hkv) * d].view(t, hkv, d),
+            qkv[:, (hq + hkv) * d:].view(t, hkv, d))
+
+
+def test_qk_norm_rope_paged_write(nqt, cuda):
+    tokens, hq, hkv, d, P, pages = 40, 16, 8, 128, 16, 12
+    qkv, qw, kw = _qk_inputs(tokens, hq, hkv, d, 11)
+    g = torch.Generator().manual_seed(12)
+    positions = torch.randint(0, 4096, (tokens,), generator=g)
+    slots = torch.randperm(pages * P, generator=g)[:tokens]
+    wp, wo = slots // P, slots % P
+    cache = torch.zeros(pages, 2, P, hkv, d, dtype=torch.bfloat16)
+    q_cpu, k_cpu, v_cpu = _split(qkv.clone(), hq, hkv, d)
+    oatt.qk_norm_rope_paged_(q_cpu, k_cpu, v_cpu, qw, kw, positions, 1e-6, 1e6, cache, wp, wo)
+    qkv_dev = qkv.to(cuda)
+    q, k, v = _split(qkv_dev, hq, hkv, d)
+    cache_dev = torch.zeros(pages, 2, P, hkv, d, dtype=torch.bfloat16, device=cuda)
+    nqt.paired_qk_norm_rope_paged_cache_(q, k, v, qw.to(cuda), kw.to(cuda), positions.to(cuda), 1e-6, 1e6,
+                                         cache_dev, wp.to(cuda), wo.to(cuda))
+    torch.cuda.synchronize()
+    for got, want in ((q.cpu(), q_cpu), (k.cpu(), k_cpu), (cache_dev.cpu(), cache)):
+        diff = (got.float() - want.float()).abs()
+        assert diff.max().item() <= 2.0 ** -7 and (diff > 0).float().mean().item() < 0.01
+    # V is copied bit for bit; cached K equals the in-place rotated K
+    assert torch.equal(cache_dev[wp.to(cuda), 1, wo.to(cuda)].cpu(), v_cpu)
+    assert torch.equal(cache_dev[wp.to(cuda), 0, wo.to(cuda)], k)
+
+
+def test_qk_norm_rope_dense_rounding_modes(nqt, cuda):
+    tokens, hq, hkv, d = 9, 16, 8, 64
+    for round_to_input in (True, False):
+        qkv, qw, kw = _qk_inputs(tokens, hq, hkv, d, 21)
+        positions = torch.arange(tokens) * 3
+        q_cpu, k_cpu, v_cpu = _split(qkv.clone(), hq, hkv, d)
+        kc = torch.zeros(tokens, 16, hkv, d, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        oatt.qk_norm_rope_dense_(q_cpu, k_cpu, v_cpu, qw, kw, positions, 1e-6, 1e6,
+                                 None if round_to_input else kc, vc, 5, round_to_input=round_to_input)
+        q, k, v = _split(qkv.to(cuda), hq, hkv, d)
+        kcd, vcd = kc.zero_().to(cuda), torch.zeros_like(vc, device=cuda)
+        if round_to_input:
+            nqt.paired_qk_norm_rope_(q, k, qw.to(cuda), kw.to(cuda), positions.to(cuda), 1e-6, 1e6)
+        else:
+            nqt.paired_qk_norm_rope_dense_cache_(q, k, v, qw.to(cuda), kw.to(cuda), positions.to(cuda), 1e-6, 1e6,
+                                                 kcd, vcd, 5)
+            assert torch.equal(kcd[:, 5], k) and torch.equal(vcd[:, 5].cpu(), v_cpu)
+        for got, want in ((q.cpu(), q_cpu), (k.cpu(), k_cpu)):
+            diff = (got.float() - want.float()).abs()
+            assert diff.max().item() <= 2.0 ** -7 and (diff > 0).float().mean().item() < 0.01
+
+
+def test_cp_fused_decode_matches_oracle(nqt, cuda):
+    rows, hq, hkv, d, cap = 256, 16, 8, 64, 16
+    g = torch.Generator().manual_seed(31)
+    for cache_pos in (0, 1, 7, 15):
+        qkv, qw, kw = _qk_inputs(rows, hq, hkv, d, 32 + cache_pos)
+        kc = torch.randn(rows, cap, hkv, d, generator=g).to(torch.bfloat16)
+        vc = torch.randn(rows, cap, hkv, d, generator=g).to(torch.bfloat16)
+        positions = torch.full((rows,), cache_pos, dtype=torch.long)
+        q_cpu, k_cpu, v_cpu = _split(qkv.clone(), hq, hkv, d)
+        kc_cpu, vc_cpu = kc.clone(), vc.clone()
+        oatt.qk_norm_rope_dense_(q_cpu, k_cpu, v_cpu, qw, kw, positions, 1e-6, 1e6, kc_cpu, vc_cpu, cache_pos,
+                                 round_to_input=False)
+        want = oatt.short_cache_attention(q_cpu, kc_cpu, vc_cpu, cache_pos + 1)
+        q, k, v = _split(qkv.to(cuda), hq, hkv, d)
+        kcd, vcd = kc.to(cuda), vc.to(cuda)
+        out = nqt.cp_decode_attention_(q, k, v, qw.to(cuda), kw.to(cuda), positions.to(cuda), 1e-6, 1e6, kcd, vcd,
+                                       cache_pos)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float().cpu(), want, atol=ATOL, rtol=0)
+        diff = (kcd.cpu().float() - kc_cpu.float()).abs()
+        assert diff.max().item() <= 2.0 ** -7
+        assert torch.equal(vcd.cpu(), vc_cpu)
+
+
+def test_short_cache_golden_fixture(nqt, cuda, golden):
+    g = golden("attention.pt")["short_cache"]
+    out = nqt.decode_attn_nhd_short_cache(g["q"].to(torch.bfloat16).to(cuda), g["k_cache"].to(torch.bfloat16).to(cuda),
+                                          g["v_cache"].to(torch.bfloat16).to(cuda), g["length"])
+    torch.testing.assert_close(out.float().cpu(), g["out"], atol=ATOL, rtol=0)

@@ -1,0 +1,127 @@
+"""GPU: the TalkerAttentionContext drop-in (plan / select_layer / attend) with
+host metadata from the oracle's builder and with device metadata from the
+GPU planner, eagerly and replayed from a CUDA graph."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle import planner as oplan
+from tests._paged import FakeAttention
+
+pytestmark = pytest.mark.gpu
+
+
+def _binding(nqt, cuda, storage, rows, tokens):
+    return nqt.binding_factory(storage=storage, capture_batch_size=rows, token_capacity=tokens, num_qo_heads=16,
+                               num_kv_heads=8, head_dim=128, page_size=16, total_pages=storage.shape[1],
+                               workspace=torch.empty(16, dtype=torch.uint8, device=cuda), shared_plan_state=None,
+                               device=cuda, dtype=torch.bfloat16, slot=0, metadata=None)
+
+
+def _meta(nqt, m, prefill):
+    def t(x, dt):
+        return torch.tensor(x, dtype=dt).pin_memory()
+
+    return nqt.TalkerAttentionMetadata(
+        qo_indptr=t(m["qo_indptr"], torch.int32) if prefill else None,
+        paged_kv_indptr=t(m["paged_kv_indptr"], torch.int32),
+        paged_kv_indices=t(m["paged_kv_indices"], torch.int32),
+        paged_kv_last_page_len=t(m["paged_kv_last_page_len"], torch.int32),
+        position_ids=t(m["position_ids"], torch.long),
+        write_pages=t(m["write_pages"], torch.long),
+        write_offsets=t(m["write_offsets"], torch.long),
+        padding_pages=(),
+    )
+
+
+def _oracle_attend(cache, m, q, k, v, attn, prefill):
+    q, k = q.clone(), k.clone()
+    oatt.qk_norm_rope_paged_(q, k, v, attn.q_norm.weight.cpu(), attn.k_norm.weight.cpu(),
+                             torch.tensor(m["position_ids"]), 1e-6, 1e6, cache, torch.tensor(m["write_pages"]),
+                             torch.tensor(m["write_offsets"]))
+    indptr = torch.tensor(m["paged_kv_indptr"])
+    indices = torch.tensor(m["paged_kv_indices"])
+    last = torch.tensor(m["paged_kv_last_page_len"])
+    if prefill:
+        return oatt.paged_prefill(q.float(), cache.float(), torch.tensor(m["qo_indptr"]), indptr, indices, last)
+    return oatt.paged_decode(q.float(), cache.float(), indptr, indices, last)
+
+
+def test_binding_prefill_then_decode_with_graph_replay(nqt, cuda):
+    layers, pages, P = 2, 64, 16
+    g = torch.Generator().manual_seed(0)
+    storage_cpu = torch.zeros(layers, pages, 2, P, 8, 128, dtype=torch.bfloat16)
+    storage = storage_cpu.to(cuda)
+    attn = FakeAttention((1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).to(cuda),
+                         (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).to(cuda))
+    pool = oplan.HostPagePool(pages, P, 12)
+    for r in ("a", "b", "c"):
+        pool.add_request(r)
+    # prefill 3 rows (capture 4 rows / 160 tokens)
+    m = pool.metadata(["a", "b", "c"], [40, 7, 100], 4, 160, True)
+    pre = _binding(nqt, cuda, storage, 4, 160)
+    pre.plan(_meta(nqt, m, True))
+    for layer in range(layers):
+        qkv = torch.randn(160, 32 * 128, generator=g).to(torch.bfloat16)
+        q, k, v = qkv[:, :2048].view(160, 16, 128), qkv[:, 2048:3072].view(160, 8, 128), qkv[:, 3072:].view(160, 8, 128)
+        want = _oracle_attend(storage_cpu[layer], m, q, k, v, attn, True)
+        pre.select_layer(layer)
+        qd = qkv.to(cuda)
+        got = pre.attend(attn, qd[:, :2048].view(160, 16, 128), qd[:, 2048:3072].view(160, 8, 128),
+                         qd[:, 3072:].view(160, 8, 128))
+        torch.testing.assert_close(got[:147].float().cpu(), want[:147], atol=2e-2, rtol=0)
+    for r in ("a", "b", "c"):
+        pool.publish(r)
+    torch.testing.assert_close(storage.cpu().float(), storage_cpu.float(), atol=2.0 ** -7, rtol=2.0 ** -7)
+    storage_cpu.copy_(storage.cpu())
+
+    # decode: capture attend for layer 0 once, replay with fresh metadata each step
+    dec = _binding(nqt, cuda, storage, 4, 4)
+    q_static = torch.zeros(4, 32 * 128, dtype=torch.bfloat16, device=cuda)
+    steps = []
+    for _ in range(3):
+        m = pool.metadata(["a", "b", "c"], [1, 1, 1], 4, 4, False)
+        steps.append(m)
+        for r in ("a", "b", "c"):
+            pool.publish(r)
+    dec.plan(_meta(nqt, steps[0], False))
+    dec.select_layer(0)
+
+    def step():
+        return dec.attend(attn, q_static[:, :2048].view(4, 16, 128), q_static[:, 2048:3072].view(4, 8, 128),
+                          q_static[:, 3072:].view(4, 8, 128))
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()  # warm-up (writes the step-0 token; redone below on replay)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = step()
+    for m in steps:
+        qkv = torch.randn(4, 32 * 128, generator=g).to(torch.bfloat16)
+        q, k, v = qkv[:, :2048].view(4, 16, 128), qkv[:, 2048:3072].view(4, 8, 128), qkv[:, 3072:].view(4, 8, 128)
+        want = _oracle_attend(storage_cpu[0], m, q, k, v, attn, False)
+        dec.plan(_meta(nqt, m, False))
+        q_static.copy_(qkv.to(cuda))
+        graph.replay()
+        torch.testing.assert_close(out[:3].float().cpu(), want[:3], atol=2e-2, rtol=0)
+    assert nqt.kernels.read_status(cuda) == 0
+
+
+def test_binding_rejects_oversized_metadata(nqt, cuda):
+    storage = torch.zeros(1, 8, 2, 16, 8, 128, dtype=torch.bfloat16, device=cuda)
+    b = _binding(nqt, cuda, storage, 2, 2)
+    m = nqt.TalkerAttentionMetadata(
+        qo_indptr=None, paged_kv_indptr=torch.zeros(3, dtype=torch.int32),
+        paged_kv_indices=torch.zeros(20, dtype=torch.int32), paged_kv_last_page_len=torch.ones(2, dtype=torch.int32),
+        position_ids=torch.zeros(2, dtype=torch.long), write_pages=torch.zeros(2, dtype=torch.long),
+        write_offsets=torch.zeros(2, dtype=torch.long), padding_pages=())
+    with pytest.raises(ValueError, match="exceeds its captured buffer"):
+        b.plan(m)
+    with pytest.raises(IndexError):
+        b.select_layer(1)
