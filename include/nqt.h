@@ -139,6 +139,35 @@ int nqt_decode_attention(
     int32_t* status, void* stream);
 
 /*
+ * Decode attention that allocates nothing.  No counterpart in the reference:
+ * it is the same split-KV decode as nqt_decode_attention (plan included),
+ * for callers that cannot allocate device memory and so cannot provide a
+ * workspace - e.g. a host whose device memory is owned by another runtime's
+ * allocator, or a loader that only passes pointers to buffers it already
+ * holds.  Its scratch (plan + split partials) is one fixed array inside the
+ * library, nqt_decode_noalloc_scratch_bytes() bytes (about 4.8 MB), held on
+ * every GPU that loads the library until the process exits.
+ * Limits: batch <= 1024, num_qo_heads <= 32, num_qo_heads * head_dim <= 2048;
+ * larger shapes return NQT_ERR_CAPACITY (see nqt_last_error).
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make it before any
+ * stream capture.  All calls share the array: calls that may overlap on
+ * the GPU (other streams or threads on the same device) race and must be
+ * serialised by the caller.  Inputs, outputs and status as in
+ * nqt_decode_attention.
+ */
+int nqt_decode_attention_noalloc(
+    const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+    const void* layer_cache, int total_pages, int page_size,
+    const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* last_page_len,
+    int batch, int num_qo_heads, int num_kv_heads, int head_dim, float sm_scale,
+    void* out, int64_t out_stride_tok, int64_t out_stride_head,
+    int32_t* status, void* stream);
+
+/* Size of the fixed scratch array behind nqt_decode_attention_noalloc. */
+size_t nqt_decode_noalloc_scratch_bytes(void);
+
+/*
  * Ragged causal prefill attention over paged KV.  Query rows of sequence b
  * are tokens [qo_indptr[b], qo_indptr[b+1]) and are the last qo_len
  * positions of that sequence's KV, so query i sees KV positions

@@ -56,6 +56,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         I,
         [P, L, L, P, I, I, P, P, P, I, I, I, I, I, F, P, L, L, P, Z, P, P],
     ),
+    "nqt_decode_attention_noalloc": (
+        I,
+        [P, L, L, P, I, I, P, P, P, I, I, I, I, F, P, L, L, P, P],
+    ),
+    "nqt_decode_noalloc_scratch_bytes": (Z, []),
     "nqt_prefill_attention": (
         I,
         [P, L, L, P, I, I, P, P, P, P, I, I, I, I, I, F, P, L, L, P, P],
@@ -136,6 +141,7 @@ def exported_symbols() -> list[str]:
 # kernels each entry point launches (nqt_plan_step adds the split-KV plan when given a workspace)
 KERNELS_PER_CALL = {
     "nqt_decode_attention": 2,
+    "nqt_decode_attention_noalloc": 3,
 }
 _launches = 0
 

@@ -12,6 +12,8 @@ void set_last_error(const char* what, cudaError_t err) {
   snprintf(g_last_error, sizeof(g_last_error), "%s: %s", what, cudaGetErrorString(err));
 }
 
+void set_last_message(const char* what) { snprintf(g_last_error, sizeof(g_last_error), "%s", what); }
+
 int check_launch(const char* what) {
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {

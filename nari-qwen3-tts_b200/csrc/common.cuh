@@ -22,6 +22,7 @@ namespace nqt {
 
 // ---------------------------------------------------------------- host side
 void set_last_error(const char* what, cudaError_t err);
+void set_last_message(const char* what);
 int check_launch(const char* what);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }

@@ -48,12 +48,12 @@ struct WsLayout {
   size_t total;
 };
 
-WsLayout ws_layout(int batch_cap, int hq, int d) {
+WsLayout ws_layout(int batch_cap, int hq, int d, int max_ctas = kMaxSplitCtas) {
   WsLayout w;
   w.tile_indptr = kHeaderBytes;
   w.part_lse = align_up(w.tile_indptr + 4 * static_cast<size_t>(batch_cap + 1), 256);
-  w.part_o = align_up(w.part_lse + 4 * static_cast<size_t>(2 * kMaxSplitCtas) * hq, 256);
-  w.total = align_up(w.part_o + 4 * static_cast<size_t>(2 * kMaxSplitCtas) * hq * d, 256);
+  w.part_o = align_up(w.part_lse + 4 * static_cast<size_t>(2 * max_ctas) * hq, 256);
+  w.total = align_up(w.part_o + 4 * static_cast<size_t>(2 * max_ctas) * hq * d, 256);
   return w;
 }
 
@@ -484,7 +484,7 @@ int encode_layer_map(CUtensorMap* map, const void* layer, int total_pages, int p
 }
 
 template <int D, int HPC, int STAGES>
-int launch_decode(const CUtensorMap& map, DecodeArgs a, int groups, cudaStream_t s) {
+int launch_decode(const CUtensorMap& map, DecodeArgs a, int groups, int max_ctas, cudaStream_t s) {
   using Cfg = DecodeCfg<D, HPC, STAGES>;
   static int occ = -1;
   static std::once_flag once;
@@ -496,7 +496,7 @@ int launch_decode(const CUtensorMap& map, DecodeArgs a, int groups, cudaStream_t
   });
   int n = num_sms() * occ / groups;
   if (n < 1) n = 1;
-  if (n > kMaxSplitCtas) n = kMaxSplitCtas;
+  if (n > max_ctas) n = max_ctas;
   a.n_ctas = n;
   decode_kernel<D, HPC, STAGES><<<dim3(n, groups), Cfg::kThreads, Cfg::kSmem, s>>>(map, a);
   int rc = check_launch("decode_attention");
@@ -506,10 +506,10 @@ int launch_decode(const CUtensorMap& map, DecodeArgs a, int groups, cudaStream_t
 }
 
 template <int D>
-int dispatch_hpc(const CUtensorMap& map, const DecodeArgs& a, cudaStream_t s) {
-  if (a.hkv % 4 == 0) return launch_decode<D, 4, 3>(map, a, a.hkv / 4, s);
-  if (a.hkv % 2 == 0) return launch_decode<D, 2, 4>(map, a, a.hkv / 2, s);
-  return launch_decode<D, 1, 4>(map, a, a.hkv, s);
+int dispatch_hpc(const CUtensorMap& map, const DecodeArgs& a, int max_ctas, cudaStream_t s) {
+  if (a.hkv % 4 == 0) return launch_decode<D, 4, 3>(map, a, a.hkv / 4, max_ctas, s);
+  if (a.hkv % 2 == 0) return launch_decode<D, 2, 4>(map, a, a.hkv / 2, max_ctas, s);
+  return launch_decode<D, 1, 4>(map, a, a.hkv, max_ctas, s);
 }
 
 }  // namespace
@@ -536,29 +536,34 @@ extern "C" int nqt_decode_plan(const int32_t* kv_indptr, const int32_t* last_pag
   return check_launch("decode_plan");
 }
 
-extern "C" int nqt_decode_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
-                                    const void* layer_cache, int total_pages, int page_size,
-                                    const int32_t* kv_indptr, const int32_t* kv_indices,
-                                    const int32_t* last_page_len, int batch, int batch_capacity, int num_qo_heads,
-                                    int num_kv_heads, int head_dim, float sm_scale, void* out,
-                                    int64_t out_stride_tok, int64_t out_stride_head, void* workspace,
-                                    size_t workspace_bytes, int32_t* status, void* stream) {
-  if (!q || !layer_cache || !kv_indptr || !kv_indices || !last_page_len || !out || !workspace) return NQT_ERR_ARG;
-  if (batch < 1 || batch > batch_capacity || total_pages < 1) return NQT_ERR_ARG;
+namespace {
+
+// Argument checks shared by the decode entry points.
+int check_decode_args(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const void* layer_cache,
+                      int total_pages, int page_size, const int32_t* kv_indptr, const int32_t* kv_indices,
+                      const int32_t* last_page_len, const void* out, int batch, int num_qo_heads, int num_kv_heads,
+                      int head_dim) {
+  if (!q || !layer_cache || !kv_indptr || !kv_indices || !last_page_len || !out) return NQT_ERR_ARG;
+  if (batch < 1 || total_pages < 1) return NQT_ERR_ARG;
   if (num_kv_heads < 1 || num_qo_heads % num_kv_heads) return NQT_ERR_ARG;
-  const int group = num_qo_heads / num_kv_heads;
-  if (group > 8 || num_kv_heads > 256) return NQT_ERR_UNSUPPORTED;
+  if (num_qo_heads / num_kv_heads > 8 || num_kv_heads > 256) return NQT_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return NQT_ERR_UNSUPPORTED;
   if (page_size < kTok || page_size % kTok || page_size > 256) return NQT_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(layer_cache) & 15) || (reinterpret_cast<uintptr_t>(q) & 3)) return NQT_ERR_ARG;
   if ((q_stride_tok & 1) || (q_stride_head & 1)) return NQT_ERR_ARG;
   if (static_cast<int64_t>(total_pages) * 2 >= (int64_t(1) << 31)) return NQT_ERR_UNSUPPORTED;
-  const WsLayout w = ws_layout(batch_capacity, num_qo_heads, head_dim);
-  if (workspace_bytes < w.total) return NQT_ERR_CAPACITY;
+  return NQT_OK;
+}
+
+// Attention launch over a plan already written at `base` with layout `w`.
+int run_decode(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const void* layer_cache,
+               int total_pages, int page_size, const int32_t* kv_indptr, const int32_t* kv_indices,
+               const int32_t* last_page_len, int batch, int num_qo_heads, int num_kv_heads, int head_dim,
+               float sm_scale, void* out, int64_t out_stride_tok, int64_t out_stride_head, uint8_t* base,
+               const WsLayout& w, int max_ctas, int32_t* status, cudaStream_t s) {
   CUtensorMap map;
   int rc = encode_layer_map(&map, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
   if (rc != NQT_OK) return rc;
-  uint8_t* base = static_cast<uint8_t*>(workspace);
   DecodeArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.q_st = q_stride_tok;
@@ -577,11 +582,124 @@ extern "C" int nqt_decode_attention(const void* q, int64_t q_stride_tok, int64_t
   a.batch = batch;
   a.hq = num_qo_heads;
   a.hkv = num_kv_heads;
-  a.group = group;
+  a.group = num_qo_heads / num_kv_heads;
   a.page_size = page_size;
   a.total_pages = total_pages;
   a.n_ctas = 1;
   a.scale_log2 = sm_scale * 1.4426950408889634f;
+  return head_dim == 128 ? dispatch_hpc<128>(map, a, max_ctas, s) : dispatch_hpc<64>(map, a, max_ctas, s);
+}
+
+}  // namespace
+
+extern "C" int nqt_decode_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                                    const void* layer_cache, int total_pages, int page_size,
+                                    const int32_t* kv_indptr, const int32_t* kv_indices,
+                                    const int32_t* last_page_len, int batch, int batch_capacity, int num_qo_heads,
+                                    int num_kv_heads, int head_dim, float sm_scale, void* out,
+                                    int64_t out_stride_tok, int64_t out_stride_head, void* workspace,
+                                    size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = check_decode_args(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr,
+                             kv_indices, last_page_len, out, batch, num_qo_heads, num_kv_heads, head_dim);
+  if (rc != NQT_OK) return rc;
+  if (!workspace || batch > batch_capacity) return NQT_ERR_ARG;
+  const WsLayout w = ws_layout(batch_capacity, num_qo_heads, head_dim);
+  if (workspace_bytes < w.total) return NQT_ERR_CAPACITY;
+  return run_decode(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr, kv_indices,
+                    last_page_len, batch, num_qo_heads, num_kv_heads, head_dim, sm_scale, out, out_stride_tok,
+                    out_stride_head, static_cast<uint8_t*>(workspace), w, kMaxSplitCtas, status,
+                    as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention with library-owned scratch, for callers that cannot
+// allocate device memory.
+//
+// Some hosts of this library must not call cudaMalloc on the serving path: a
+// loader that only hands out pointers to buffers it already owns, a process
+// whose allocator is held by another runtime, or code running where an
+// allocation could block or fail at the wrong time.  They still need the
+// split-KV plan and the per-split partial results somewhere.  This entry
+// point keeps them in one fixed array compiled into the library: every GPU
+// that loads libnqt holds kNoAllocScratchBytes of it until the process exits.
+//
+// Host code cannot use the array's name as a device address (on the host
+// the name is a stand-in, not the device buffer), so the address is looked
+// up once per device with cudaGetSymbolAddress, with that device current,
+// on the first call made on it; make that first call before any stream
+// capture.  Nothing in the array has to start at zero: each call rewrites
+// the plan before the attention kernels read it.  All calls share the
+// array, so two calls that can overlap on the GPU (different streams, or
+// different threads on one device) race on it; serialise them.
+namespace {
+
+constexpr int kNoAllocMaxBatch = 1024;     // rows per call
+constexpr int kNoAllocMaxHeads = 32;       // num_qo_heads
+constexpr int kNoAllocMaxHeadsDim = 2048;  // num_qo_heads * head_dim
+constexpr int kNoAllocMaxCtas = 296;       // split CTAs per KV-head group (2 per SM on 148 SMs)
+constexpr size_t kNoAllocScratchBytes =
+    kHeaderBytes + 4352 + 256 + 4ull * 2 * kNoAllocMaxCtas * kNoAllocMaxHeads + 256 +
+    4ull * 2 * kNoAllocMaxCtas * kNoAllocMaxHeadsDim;  // header + tile prefix + lse + partial O (about 4.8 MB)
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up once per device).
+int noalloc_scratch(uint8_t** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) {
+    set_last_error("nqt_decode_attention_noalloc: cudaGetDevice", err);
+    return NQT_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return NQT_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess || p == nullptr) {
+      set_last_error("nqt_decode_attention_noalloc: cudaGetSymbolAddress", err);
+      return NQT_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = static_cast<uint8_t*>(g_noalloc_ptr[dev]);
+  return NQT_OK;
+}
+
+}  // namespace
+
+extern "C" size_t nqt_decode_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int nqt_decode_attention_noalloc(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                                            const void* layer_cache, int total_pages, int page_size,
+                                            const int32_t* kv_indptr, const int32_t* kv_indices,
+                                            const int32_t* last_page_len, int batch, int num_qo_heads,
+                                            int num_kv_heads, int head_dim, float sm_scale, void* out,
+                                            int64_t out_stride_tok, int64_t out_stride_head, int32_t* status,
+                                            void* stream) {
+  int rc = check_decode_args(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr,
+                             kv_indices, last_page_len, out, batch, num_qo_heads, num_kv_heads, head_dim);
+  if (rc != NQT_OK) return rc;
+  if (batch > kNoAllocMaxBatch || num_qo_heads > kNoAllocMaxHeads || num_qo_heads * head_dim > kNoAllocMaxHeadsDim) {
+    set_last_message("nqt_decode_attention_noalloc: shape beyond the fixed scratch (batch <= 1024, "
+                     "num_qo_heads <= 32, num_qo_heads * head_dim <= 2048)");
+    return NQT_ERR_CAPACITY;
+  }
+  const WsLayout w = ws_layout(batch, num_qo_heads, head_dim, kNoAllocMaxCtas);
+  if (w.total > kNoAllocScratchBytes) return NQT_ERR_CAPACITY;
+  uint8_t* base = nullptr;
+  rc = noalloc_scratch(&base);
+  if (rc != NQT_OK) return rc;
   cudaStream_t s = as_stream(stream);
-  return head_dim == 128 ? dispatch_hpc<128>(map, a, s) : dispatch_hpc<64>(map, a, s);
+  decode_plan_kernel<<<1, 1024, 0, s>>>(kv_indptr, last_page_len, batch, page_size, reinterpret_cast<int32_t*>(base),
+                                        reinterpret_cast<int32_t*>(base + w.tile_indptr));
+  rc = check_launch("nqt_decode_attention_noalloc: plan");
+  if (rc != NQT_OK) return rc;
+  return run_decode(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr, kv_indices,
+                    last_page_len, batch, num_qo_heads, num_kv_heads, head_dim, sm_scale, out, out_stride_tok,
+                    out_stride_head, base, w, kNoAllocMaxCtas, status, s);
 }
