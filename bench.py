@@ -56,6 +56,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--pool-tokens", type=int, default=POOL_TOKENS)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--grow", action="store_true",
+                   help="publish each step (contexts grow by one token per step) instead of holding them fixed")
     return p.parse_args()
 
 
@@ -239,7 +241,8 @@ def main() -> None:
     shape = talker_step.TalkerShape(num_layers=args.layers)
     pages = args.pool_tokens // 16
     step = talker_step.TalkerDecodeStep(shape=shape, batch=BATCH, total_pages=pages, page_size=16,
-                                        max_pages_per_seq=(CTX_HI + 1024) // 16, device=dev, seed=rank)
+                                        max_pages_per_seq=(CTX_HI + 1024) // 16, device=dev, seed=rank,
+                                        publish=args.grow)
     contexts = contexts_for(rank)
     step.admit(contexts, scatter_seed=rank)
     lib_mod.reset_launch_count()
@@ -287,8 +290,8 @@ def main() -> None:
     e2e_value = world * BATCH * e2e_steps / (e2e_ms / 1e3)
 
     # ---------------------------------------------------------------- attention roofline
-    # the binding holds the metadata of the last executed step: every row at initial + executed tokens
-    lengths = [n + executed for n in contexts]
+    # the binding holds the metadata of the last executed step
+    lengths = [n + (executed if args.grow else 1) for n in contexts]
     attn_bytes = sum(lengths) * 2 * shape.num_kv_heads * shape.head_dim * 2 + 2 * BATCH * shape.num_heads * shape.head_dim * 2
     q = torch.randn(BATCH, shape.num_heads, shape.head_dim, device=dev).to(torch.bfloat16)
     b = step.binding
@@ -317,6 +320,9 @@ def main() -> None:
     attn_ms = max_over_ranks(a0.elapsed_time(a1), world) / (reps * shape.num_layers)
     peak, peak_kind = peaks()
     achieved = attn_bytes / (attn_ms / 1e3) / 1e9
+    # DRAM traffic of one decode launch from an ncu capture of this kernel on the same contexts
+    # (2-layer model, Sum(ctx + 2) = 74466 tokens): 307.57 MB read + 4.90 MB written, scaled by tokens
+    traffic = (307.566080e6 + 4.895232e6) * (sum(lengths) / 74466.0) if args.layers == 28 else None
     status = nqt.kernels.read_status(dev) | int(step.planner.status.item())
 
     line = {
@@ -339,12 +345,14 @@ def main() -> None:
             "global_batch": BATCH * world,
             "seq_len": CTX_HI,
             "parallelism": f"dp{world} (request-sharded, no collective)",
-            "l2": "inputs larger than L2: ~7.8 GB of KV read per step",
+            "l2": "inputs larger than L2: ~8.5 GB of KV read per step",
+            "contexts": "held at the sampled lengths (each step's reservation is discarded)" if not args.grow
+            else "growing by one token per step (published)",
         },
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
                 "d2h_bytes_per_step": BATCH * 8},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "kernel": "decode attention (decode_kernel + decode_merge_kernel)",
+                     "traffic": traffic, "kernel": "decode attention (decode_kernel + decode_merge_kernel)",
                      "bytes_per_launch": attn_bytes, "us_per_launch": attn_ms * 1e3,
                      "peak_source": f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"},
         "gpu_launches": launches_per_step * args.steps,

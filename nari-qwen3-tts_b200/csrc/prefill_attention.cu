@@ -18,6 +18,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace nqt {
 namespace {
@@ -312,6 +313,322 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) prefill_kernel(const __
   }
 }
 
+// ------------------------------------------------------------------ tcgen05 path (D = 128)
+// CTA = 128 query rows (token x GQA head) x one KV head; KV blocks of 64 tokens.
+//   warp 0      TMA producer (Q once, then K and V of each block)
+//   warp 1      TMEM allocator and the single MMA-issuing thread
+//   warps 2..5  softmax: thread = one query row = one TMEM lane
+// TMEM columns: S double buffer [0, 64) and [64, 128) (fp32), O [128, 256) (fp32).
+// S = Q K^T: A = Q (K-major, 128B swizzle), B = K (K-major); O += P V: A = P
+// (bf16, written by the softmax threads into a swizzled SMEM tile, K-major),
+// B = V (MN-major: token rows of 64 contiguous dims).  O is rescaled in TMEM
+// only when a row's running max grows by more than 2^8 (exact either way:
+// the exponent base only has to be shared by P and l).
+namespace tcp {
+constexpr int kM = 128;
+constexpr int kN = 64;
+constexpr int kStages = 3;
+constexpr int kQBytes = kM * 128 * 2;           // [half][128 rows][128 B]
+constexpr int kKVHalf = kN * 128;               // [64 tokens][128 B]
+constexpr int kKVBytes = 4 * kKVHalf;           // K h0, K h1, V h0, V h1
+constexpr int kPBytes = kM * kN * 2;            // [128 rows][128 B]
+constexpr int kThreads = 6 * 32;
+constexpr int kBarBytes = 256;
+constexpr int kSmem = 1024 + kQBytes + kStages * kKVBytes + 2 * kPBytes + kBarBytes;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColO = 128;
+}  // namespace tcp
+
+__global__ void __launch_bounds__(tcp::kThreads, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kvmap,
+                      PrefillArgs p) {
+  using namespace tcp;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + kQBytes;
+  uint8_t* sP = sKV + kStages * kKVBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + kStages;
+  uint64_t* s_full = kv_empty + kStages;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* o_done = p_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  int* info = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kvh = blockIdx.y;
+  const int G = p.group;
+  const int tpt = kM / G;
+  if (threadIdx.x == 0) {
+    int remaining = blockIdx.x, seq = -1, tile = 0;
+    for (int b = 0; b < p.batch; ++b) {
+      const int qo = p.qo_indptr[b + 1] - p.qo_indptr[b];
+      const int tiles = qo > 0 ? (qo + tpt - 1) / tpt : 0;
+      if (remaining < tiles) {
+        seq = b;
+        tile = remaining;
+        break;
+      }
+      remaining -= tiles;
+    }
+    info[0] = seq;
+    info[1] = tile;
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], 4);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&o_done[b], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const int seq = info[0];
+
+  int nb = 0, q0 = 0, qo_len = 0, n_pages = 0, kv_len = 0, t_first = 0, shift = 0;
+  if (seq >= 0) {
+    q0 = p.qo_indptr[seq];
+    qo_len = p.qo_indptr[seq + 1] - q0;
+    n_pages = p.kv_indptr[seq + 1] - p.kv_indptr[seq];
+    int ll = p.last_len[seq];
+    ll = ll < 1 ? 1 : (ll > p.page_size ? p.page_size : ll);
+    kv_len = n_pages > 0 ? (n_pages - 1) * p.page_size + ll : 0;
+    t_first = info[1] * tpt;
+    const int t_last = min(qo_len, t_first + tpt) - 1;
+    shift = kv_len - qo_len;
+    const int kv_hi = min(kv_len, shift + t_last + 1);
+    nb = kv_hi > 0 ? (kv_hi + kN - 1) / kN : 0;
+  }
+
+  if (nb > 0) {
+    if (warp == 0) {
+      // ------------------------------------------------------------ producer
+      if (lane == 0) {
+        prefetch_tensormap(&qmap);
+        prefetch_tensormap(&kvmap);
+        mbar_arrive_expect_tx(q_full, kQBytes);
+        for (int half = 0; half < 2; ++half)
+          tma_load_3d(sQ + half * (kQBytes / 2), &qmap, q_full, half * 64, kvh * G, q0 + t_first);
+        const int32_t* pages = p.indices + p.kv_indptr[seq];
+        for (int j = 0; j < nb; ++j) {
+          const int s = j % kStages;
+          if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.status)) break;
+          mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
+          uint8_t* st = sKV + s * kKVBytes;
+#pragma unroll
+          for (int sub = 0; sub < kN / 16; ++sub) {
+            const int pos = j * kN + sub * 16;
+            const int pi = pos / p.page_size;
+            int page = p.total_pages;  // past the sequence: zero-filled box
+            if (pi < n_pages) {
+              page = pages[pi];
+              if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.total_pages)) {
+                report(p.status, NQT_DEV_BAD_PAGE);
+                page = p.total_pages;
+              }
+            }
+            const int tip = pos - pi * p.page_size;
+#pragma unroll
+            for (int kind = 0; kind < 2; ++kind)
+#pragma unroll
+              for (int half = 0; half < 2; ++half)
+                tma_load_4d(st + (kind * 2 + half) * kKVHalf + sub * 2048, &kvmap, &kv_full[s], half * 64, kvh, tip,
+                            page * 2 + kind);
+          }
+        }
+      }
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t kIdescS = tc::idesc_bf16_f32(kM, kN, false, false);
+        constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(kM, 128, false, true);
+        bool ok = mbar_wait(q_full, 0, p.status);
+        auto issue_pv = [&](int i) {
+          const int sb = i & 1, s = i % kStages;
+          if (!mbar_wait(&p_full[sb], (i >> 1) & 1, p.status)) {
+            ok = false;
+            return;
+          }
+          tc::fence_after_sync();
+          const uint32_t p_addr = smem_addr(sP + sb * kPBytes);
+          const uint32_t v_addr = smem_addr(sKV + s * kKVBytes + 2 * kKVHalf);
+#pragma unroll
+          for (int ks = 0; ks < kN / 16; ++ks) {
+            const uint64_t a = tc::smem_desc_sw128(p_addr + ks * 32, 16, 1024);
+            const uint64_t b = tc::smem_desc_sw128(v_addr + ks * 2048, kKVHalf, 1024);
+            tc::mma_f16_ss(tmem + kColO, a, b, kIdescPV, (i > 0 || ks > 0) ? 1u : 0u);
+          }
+          tc::commit(&kv_empty[s]);
+          tc::commit(&o_done[sb]);
+        };
+        const uint32_t q_addr = smem_addr(sQ);
+        for (int j = 0; j < nb && ok; ++j) {
+          const int s = j % kStages, sb = j & 1;
+          if (!mbar_wait(&kv_full[s], (j / kStages) & 1, p.status)) break;
+          if (j >= 2 && !mbar_wait(&s_free[sb], ((j - 2) >> 1) & 1, p.status)) break;
+          tc::fence_after_sync();
+          const uint32_t k_addr = smem_addr(sKV + s * kKVBytes);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32;
+            const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
+            const uint64_t a = tc::smem_desc_sw128(q_addr + off, 16, 1024);
+            const uint64_t b = tc::smem_desc_sw128(k_addr + koff, 16, 1024);
+            tc::mma_f16_ss(tmem + sb * kN, a, b, kIdescS, kk > 0 ? 1u : 0u);
+          }
+          tc::commit(&s_full[sb]);
+          if (j >= 1) issue_pv(j - 1);
+        }
+        if (ok) issue_pv(nb - 1);
+      }
+    } else {
+      // ------------------------------------------------------------ softmax warps
+      const int quarter = warp & 3;
+      const int row = quarter * 32 + lane;
+      const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int qtok = t_first + row / G;
+      const int head = kvh * G + row % G;
+      const int lim = shift + qtok;
+      const float NEG_INF = -__int_as_float(0x7f800000);
+      float m_used = NEG_INF, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < nb && ok; ++j) {
+        const int sb = j & 1;
+        const int s = j % kStages;
+        if (!mbar_wait(&s_full[sb], (j >> 1) & 1, p.status)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        uint32_t sr[64];
+        tc::ld_32x32b_x32(t_row + sb * kN, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tc::ld_32x32b_x32(t_row + sb * kN + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        tc::wait_ld();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[sb]);
+        const int base = j * kN;
+        float mx = NEG_INF;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const int key = base + c;
+          const float v = (key <= lim && key < kv_len) ? __uint_as_float(sr[c]) * p.scale_log2 : NEG_INF;
+          sr[c] = __float_as_uint(v);
+          mx = fmaxf(mx, v);
+        }
+        const float m_new = fmaxf(m_used, mx);
+        const bool need = (m_used != NEG_INF) && (m_new > m_used + 8.f);
+        if (__any_sync(kFull, need)) {
+          // rescale this warp's O rows once PV(j-1) has landed
+          if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const float alpha = need ? exp2f(m_used - m_new) : 1.f;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            uint32_t o[32];
+            tc::ld_32x32b_x32(t_row + kColO + ch * 32, o);
+            tc::wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tc::st_32x32b_x32(t_row + kColO + ch * 32, o);
+          }
+          tc::wait_st();
+          if (need) {
+            l *= alpha;
+            m_used = m_new;
+          }
+        }
+        if (m_used == NEG_INF) m_used = m_new;
+        // the P buffer of this parity is free once PV(j-2) has completed
+        if (j >= 2 && !mbar_wait(&o_done[sb], ((j - 2) >> 1) & 1, p.status)) {
+          ok = false;
+          break;
+        }
+        uint8_t* prow = sP + sb * kPBytes + row * 128;
+        float rs = 0.f;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = exp2f(__uint_as_float(sr[c8 * 8 + 2 * e]) - m_used);
+            const float p1 = exp2f(__uint_as_float(sr[c8 * 8 + 2 * e + 1]) - m_used);
+            rs += p0 + p1;
+            w[e] = pack_bf16x2(p0, p1);
+          }
+          *reinterpret_cast<uint4*>(prow + ((c8 ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        l += rs;
+        if (base + kN > kv_len) {
+          // zero V rows at or past kv_len so 0 * stale never meets a NaN
+          const int first_bad = max(0, kv_len - base);
+          const int n_bad = kN - first_bad;
+          uint8_t* v0 = sKV + s * kKVBytes + 2 * kKVHalf;
+          for (int idx = row; idx < n_bad * 16; idx += 128) {
+            const int t = first_bad + (idx >> 4);
+            const int half = (idx >> 3) & 1, chunk = idx & 7;
+            *reinterpret_cast<uint4*>(v0 + half * kKVHalf + t * 128 + chunk * 16) = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[sb]);
+      }
+      // epilogue: O / l once the last PV has completed
+      if (ok && mbar_wait(&o_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, p.status)) {
+        tc::fence_after_sync();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const bool store = qtok < qo_len;
+        __nv_bfloat16* orow =
+            p.out + static_cast<int64_t>(q0 + qtok) * p.o_st + static_cast<int64_t>(head) * p.o_sh;
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t o[32];
+          tc::ld_32x32b_x32(t_row + kColO + ch * 32, o);
+          tc::wait_ld();
+          if (store) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 pk;
+              pk.x = pack_bf16x2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
+              pk.y = pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
+              pk.z = pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
+              pk.w = pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + ch * 32 + v * 8) = pk;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -338,6 +655,48 @@ int encode_map(CUtensorMap* map, const void* layer, int total_pages, int page_si
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? NQT_OK : NQT_ERR_CUDA;
+}
+
+// K-only or V-only boxes {64 dims, 1 head, 16 tokens, 1 kind} for the tcgen05 path.
+int encode_kv_map_single(CUtensorMap* map, const void* layer, int total_pages, int page_size, int hkv, int d) {
+  auto encode = get_encode();
+  if (encode == nullptr) return NQT_ERR_CUDA;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(hkv),
+                        static_cast<cuuint64_t>(page_size), static_cast<cuuint64_t>(total_pages) * 2};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(d) * 2, static_cast<cuuint64_t>(hkv) * d * 2,
+                           static_cast<cuuint64_t>(page_size) * hkv * d * 2};
+  cuuint32_t box[4] = {64, 1, kTok, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(layer), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NQT_OK : NQT_ERR_CUDA;
+}
+
+// Q viewed as {D, heads, tokens}; one box = 64 dims x G heads x (128 / G) tokens = 128 rows of 128 B.
+int encode_q_map(CUtensorMap* map, const void* q, int64_t q_st, int64_t q_sh, int tokens, int hq, int group) {
+  auto encode = get_encode();
+  if (encode == nullptr) return NQT_ERR_CUDA;
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(hq), static_cast<cuuint64_t>(tokens)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(q_sh) * 2, static_cast<cuuint64_t>(q_st) * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(group), static_cast<cuuint32_t>(tcp::kM / group)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NQT_OK : NQT_ERR_CUDA;
+}
+
+int launch_prefill_tc(const CUtensorMap& qmap, const CUtensorMap& kvmap, const PrefillArgs& a, int total_q,
+                      cudaStream_t s) {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tcp::kSmem);
+  });
+  const int tpt = tcp::kM / a.group;
+  const int grid_x = (total_q + tpt - 1) / tpt + a.batch;
+  prefill_tc_kernel<<<dim3(grid_x, a.hkv), tcp::kThreads, tcp::kSmem, s>>>(qmap, kvmap, a);
+  return check_launch("prefill_attention_tc");
 }
 
 template <int D, int STAGES>
@@ -376,9 +735,6 @@ extern "C" int nqt_prefill_attention(const void* q, int64_t q_stride_tok, int64_
   if ((q_stride_tok & 1) || (q_stride_head & 1) || (out_stride_tok & 1) || (out_stride_head & 1)) return NQT_ERR_ARG;
   if (static_cast<int64_t>(total_pages) * 2 >= (int64_t(1) << 31)) return NQT_ERR_UNSUPPORTED;
   if (total_q_tokens == 0) return NQT_OK;
-  CUtensorMap map;
-  int rc = encode_map(&map, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
-  if (rc != NQT_OK) return rc;
   PrefillArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.q_st = q_stride_tok;
@@ -398,8 +754,21 @@ extern "C" int nqt_prefill_attention(const void* q, int64_t q_stride_tok, int64_
   a.page_size = page_size;
   a.total_pages = total_pages;
   a.scale_log2 = sm_scale * 1.4426950408889634f;
+  cudaStream_t s = as_stream(stream);
+  if (head_dim == 128) {
+    // tcgen05 path: Q rows come in by TMA, so q must be 16-byte aligned with strides in 16-byte units
+    if ((reinterpret_cast<uintptr_t>(q) & 15) || (q_stride_tok % 8) || (q_stride_head % 8)) return NQT_ERR_ARG;
+    CUtensorMap qmap, kvmap;
+    int rc = encode_q_map(&qmap, q, q_stride_tok, q_stride_head, total_q_tokens, num_qo_heads, group);
+    if (rc != NQT_OK) return rc;
+    rc = encode_kv_map_single(&kvmap, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
+    if (rc != NQT_OK) return rc;
+    return launch_prefill_tc(qmap, kvmap, a, total_q_tokens, s);
+  }
+  CUtensorMap map;
+  int rc = encode_map(&map, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
+  if (rc != NQT_OK) return rc;
   const int tokens_per_tile = kRows / group;
   const int grid_x = (total_q_tokens + tokens_per_tile - 1) / tokens_per_tile + batch;
-  cudaStream_t s = as_stream(stream);
-  return head_dim == 128 ? launch_prefill<128, 3>(map, a, grid_x, s) : launch_prefill<64, 4>(map, a, grid_x, s);
+  return launch_prefill<64, 4>(map, a, grid_x, s);
 }

@@ -77,8 +77,12 @@ class TalkerDecodeStep:
         max_pages_per_seq: int = 512,
         device: torch.device | str = "cuda",
         seed: int = 0,
+        publish: bool = True,
     ) -> None:
         self.shape = s = shape
+        # publish=False discards each step's reservation after the step, so every
+        # step sees the same context lengths (a stationary benchmark workload)
+        self.publish = publish
         self.batch = batch
         self.page_size = page_size
         self.device = dev = torch.device(device)
@@ -189,7 +193,7 @@ class TalkerDecodeStep:
         sample_rows(logits, self.temperature, self.top_k, self.top_p, self.seed, self.offset,
                     repetition_penalty=self.penalty, seen_token_mask=self.seen, update_seen=True,
                     round_scaled_to_input=False, out=self.tokens)
-        self.planner.commit(True)
+        self.planner.commit(self.publish)
         self.offset.add_(FRAME_OFFSET_STRIDE)
         return self.tokens
 
