@@ -143,12 +143,14 @@ __device__ __forceinline__ int find_seq(const int32_t* tile_indptr, int batch, i
   return lo;
 }
 
+constexpr int kSmemPrefix = 1024;  // tile_indptr entries staged in shared memory (batch + 1 <= this)
+
 template <int D, int HPC, int STAGES>
 struct DecodeCfg {
   static constexpr int kHalves = D / 64;
   static constexpr int kStageBytes = HPC * kHalves * kBoxBytes;
   static constexpr int kThreads = (HPC + 1) * 32;
-  static constexpr int kSmem = STAGES * kStageBytes + 1024 + 2 * STAGES * 8;
+  static constexpr int kSmem = STAGES * kStageBytes + 1024 + 2 * STAGES * 8 + 4 * kSmemPrefix;
 };
 
 template <int D, int HPC, int STAGES>
@@ -160,6 +162,7 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::kStageBytes);
   uint64_t* empty = full + STAGES;
+  int32_t* s_prefix = reinterpret_cast<int32_t*>(empty + STAGES);
 
   const int c = blockIdx.x;
   const int kv0 = blockIdx.y * HPC;
@@ -173,6 +176,11 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   const int tpp = p.page_size / kTok;
   const int n_tiles = static_cast<int>(t_end - t_begin);
 
+  // one parallel load of the per-sequence tile prefix instead of a chain of dependent loads
+  const bool staged = p.batch + 1 <= kSmemPrefix;
+  if (staged)
+    for (int b = threadIdx.x; b <= p.batch; b += blockDim.x) s_prefix[b] = p.tile_indptr[b];
+  const int32_t* prefix = staged ? s_prefix : p.tile_indptr;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -186,15 +194,15 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
     // ---------------------------------------------------------- producer
     if (lane == 0) {
       prefetch_tensormap(&tmap);
-      int seq = find_seq(p.tile_indptr, p.batch, t_begin);
-      int seq_t0 = p.tile_indptr[seq];
-      int seq_t1 = p.tile_indptr[seq + 1];
+      int seq = find_seq(prefix, p.batch, t_begin);
+      int seq_t0 = prefix[seq];
+      int seq_t1 = prefix[seq + 1];
       for (int i = 0; i < n_tiles; ++i) {
         const int64_t t = t_begin + i;
         while (t >= seq_t1) {  // advance to the owning sequence (skips empty rows)
           ++seq;
           seq_t0 = seq_t1;
-          seq_t1 = p.tile_indptr[seq + 1];
+          seq_t1 = prefix[seq + 1];
         }
         const int s = i % STAGES;
         if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, p.status)) break;
@@ -230,9 +238,9 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   float o[D / 16][4];
   float m0 = NEG_INF, m1 = NEG_INF, l0 = 0.f, l1 = 0.f;
 
-  int seq = find_seq(p.tile_indptr, p.batch, t_begin);
-  int seq_t0 = p.tile_indptr[seq];
-  int seq_t1 = p.tile_indptr[seq + 1];
+  int seq = find_seq(prefix, p.batch, t_begin);
+  int seq_t0 = prefix[seq];
+  int seq_t1 = prefix[seq + 1];
   bool seg_open = false;
 
   // ldmatrix lane roles
@@ -244,7 +252,7 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
     while (t >= seq_t1) {
       ++seq;
       seq_t0 = seq_t1;
-      seq_t1 = p.tile_indptr[seq + 1];
+      seq_t1 = prefix[seq + 1];
     }
     if (!seg_open) {
       // new segment: load this sequence's query heads of the group as B fragments
@@ -417,41 +425,68 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
 }
 
 // ------------------------------------------------------------------ merge
+// One CTA per sequence; sequences that one CTA covered whole exit at once.  Thread
+// (head, 4 dims) combines the split partials: out = sum_i w_i O_i / sum_i w_i,
+// w_i = 2^(lse_i - max lse); the loads of up to 16 contributors are issued together.
 template <int D>
-__global__ void __launch_bounds__(D) decode_merge_kernel(DecodeArgs p) {
+__global__ void __launch_bounds__(512) decode_merge_kernel(DecodeArgs p) {
+  constexpr int kBatch = 16;
   const int seq = blockIdx.x;
-  const int head = blockIdx.y;
-  const int d = threadIdx.x;
   const int64_t total = p.header[0];
   const int n = p.n_ctas;
   const int64_t tb0 = p.tile_indptr[seq];
   const int64_t tb1 = p.tile_indptr[seq + 1];
-  __nv_bfloat16* ob = p.out + seq * p.o_st + static_cast<int64_t>(head) * p.o_sh;
-  if (tb1 <= tb0) {
-    ob[d] = __float2bfloat16_rn(0.f);
+  if (tb1 <= tb0) {  // a row with no pages: defined output of zeros
+    for (int i = threadIdx.x; i < p.hq * D; i += blockDim.x)
+      p.out[seq * p.o_st + static_cast<int64_t>(i / D) * p.o_sh + i % D] = __float2bfloat16_rn(0.f);
     return;
   }
   // CTA owning tile t: max c with floor(total*c/n) <= t
   const int c0 = static_cast<int>(((tb0 + 1) * n + total - 1) / total) - 1;
   const int c1 = static_cast<int>((tb1 * n + total - 1) / total) - 1;
   if (c0 == c1) return;  // written directly by the decode kernel
-  float mx = -__int_as_float(0x7f800000);
-  for (int c = c0; c <= c1; ++c) {
-    const int64_t st = range_start(total, c, n);
-    if (st == range_start(total, c + 1, n)) continue;  // a CTA with no tiles left no partial
-    const int slot = (st >= tb0) ? 2 * c : 2 * c + 1;
-    mx = fmaxf(mx, p.part_lse[static_cast<int64_t>(slot) * p.hq + head]);
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  for (int idx = threadIdx.x; idx < p.hq * (D / 4); idx += blockDim.x) {
+    const int h = idx / (D / 4);
+    const int d = (idx % (D / 4)) * 4;
+    float mx = NEG_INF, wsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int cb = c0; cb <= c1; cb += kBatch) {
+      int slot[kBatch];
+      float lse[kBatch];
+      float4 v[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int cc = cb + k;
+        slot[k] = -1;
+        if (cc <= c1) {
+          const int64_t st = range_start(total, cc, n);
+          if (st != range_start(total, cc + 1, n)) slot[k] = (st >= tb0) ? 2 * cc : 2 * cc + 1;
+        }
+        const int64_t sl = slot[k] >= 0 ? slot[k] : 0;
+        lse[k] = slot[k] >= 0 ? p.part_lse[sl * p.hq + h] : NEG_INF;
+        v[k] = *reinterpret_cast<const float4*>(p.part_o + (sl * p.hq + h) * D + d);
+      }
+      float bm = NEG_INF;
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) bm = fmaxf(bm, lse[k]);
+      const float nm = fmaxf(mx, bm);
+      const float sc = mx == NEG_INF ? 0.f : exp2f(mx - nm);
+      wsum *= sc;
+      acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const float w = slot[k] >= 0 ? exp2f(lse[k] - nm) : 0.f;
+        wsum += w;
+        acc.x += w * v[k].x; acc.y += w * v[k].y; acc.z += w * v[k].z; acc.w += w * v[k].w;
+      }
+      mx = nm;
+    }
+    const float inv = 1.f / wsum;
+    __nv_bfloat16* ob = p.out + seq * p.o_st + static_cast<int64_t>(h) * p.o_sh + d;
+    *reinterpret_cast<__nv_bfloat162*>(ob) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+    *reinterpret_cast<__nv_bfloat162*>(ob + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
   }
-  float wsum = 0.f, acc = 0.f;
-  for (int c = c0; c <= c1; ++c) {
-    const int64_t st = range_start(total, c, n);
-    if (st == range_start(total, c + 1, n)) continue;
-    const int slot = (st >= tb0) ? 2 * c : 2 * c + 1;
-    const float w = exp2f(p.part_lse[static_cast<int64_t>(slot) * p.hq + head] - mx);
-    wsum += w;
-    acc += w * p.part_o[(static_cast<int64_t>(slot) * p.hq + head) * D + d];
-  }
-  ob[d] = __float2bfloat16_rn(acc / wsum);
 }
 
 // ------------------------------------------------------------------ host
@@ -501,13 +536,23 @@ int launch_decode(const CUtensorMap& map, DecodeArgs a, int groups, int max_ctas
   decode_kernel<D, HPC, STAGES><<<dim3(n, groups), Cfg::kThreads, Cfg::kSmem, s>>>(map, a);
   int rc = check_launch("decode_attention");
   if (rc != NQT_OK) return rc;
-  decode_merge_kernel<D><<<dim3(a.batch, a.hq, 1), D, 0, s>>>(a);
+  decode_merge_kernel<D><<<a.batch, 256, 0, s>>>(a);
   return check_launch("decode_merge");
 }
 
+// KV heads per CTA and TMA pipeline depth of the widest configuration (4 heads: 32 KB stages,
+// 3 stages -> 2 CTAs per SM).
+#ifndef NQT_DECODE_HPC
+#define NQT_DECODE_HPC 4
+#endif
+#ifndef NQT_DECODE_STAGES
+#define NQT_DECODE_STAGES 3
+#endif
+
 template <int D>
 int dispatch_hpc(const CUtensorMap& map, const DecodeArgs& a, int max_ctas, cudaStream_t s) {
-  if (a.hkv % 4 == 0) return launch_decode<D, 4, 3>(map, a, a.hkv / 4, max_ctas, s);
+  constexpr int H = NQT_DECODE_HPC;
+  if (a.hkv % H == 0) return launch_decode<D, H, NQT_DECODE_STAGES>(map, a, a.hkv / H, max_ctas, s);
   if (a.hkv % 2 == 0) return launch_decode<D, 2, 4>(map, a, a.hkv / 2, max_ctas, s);
   return launch_decode<D, 1, 4>(map, a, a.hkv, max_ctas, s);
 }
@@ -541,8 +586,8 @@ namespace {
 // Argument checks shared by the decode entry points.
 int check_decode_args(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const void* layer_cache,
                       int total_pages, int page_size, const int32_t* kv_indptr, const int32_t* kv_indices,
-                      const int32_t* last_page_len, const void* out, int batch, int num_qo_heads, int num_kv_heads,
-                      int head_dim) {
+                      const int32_t* last_page_len, const void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                      int batch, int num_qo_heads, int num_kv_heads, int head_dim) {
   if (!q || !layer_cache || !kv_indptr || !kv_indices || !last_page_len || !out) return NQT_ERR_ARG;
   if (batch < 1 || total_pages < 1) return NQT_ERR_ARG;
   if (num_kv_heads < 1 || num_qo_heads % num_kv_heads) return NQT_ERR_ARG;
@@ -551,6 +596,7 @@ int check_decode_args(const void* q, int64_t q_stride_tok, int64_t q_stride_head
   if (page_size < kTok || page_size % kTok || page_size > 256) return NQT_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(layer_cache) & 15) || (reinterpret_cast<uintptr_t>(q) & 3)) return NQT_ERR_ARG;
   if ((q_stride_tok & 1) || (q_stride_head & 1)) return NQT_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(out) & 3) || (out_stride_tok & 1) || (out_stride_head & 1)) return NQT_ERR_ARG;
   if (static_cast<int64_t>(total_pages) * 2 >= (int64_t(1) << 31)) return NQT_ERR_UNSUPPORTED;
   return NQT_OK;
 }
@@ -600,7 +646,8 @@ extern "C" int nqt_decode_attention(const void* q, int64_t q_stride_tok, int64_t
                                     int64_t out_stride_tok, int64_t out_stride_head, void* workspace,
                                     size_t workspace_bytes, int32_t* status, void* stream) {
   int rc = check_decode_args(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr,
-                             kv_indices, last_page_len, out, batch, num_qo_heads, num_kv_heads, head_dim);
+                             kv_indices, last_page_len, out, out_stride_tok, out_stride_head, batch, num_qo_heads,
+                             num_kv_heads, head_dim);
   if (rc != NQT_OK) return rc;
   if (!workspace || batch > batch_capacity) return NQT_ERR_ARG;
   const WsLayout w = ws_layout(batch_capacity, num_qo_heads, head_dim);
@@ -682,7 +729,8 @@ extern "C" int nqt_decode_attention_noalloc(const void* q, int64_t q_stride_tok,
                                             int64_t out_stride_tok, int64_t out_stride_head, int32_t* status,
                                             void* stream) {
   int rc = check_decode_args(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr,
-                             kv_indices, last_page_len, out, batch, num_qo_heads, num_kv_heads, head_dim);
+                             kv_indices, last_page_len, out, out_stride_tok, out_stride_head, batch, num_qo_heads,
+                             num_kv_heads, head_dim);
   if (rc != NQT_OK) return rc;
   if (batch > kNoAllocMaxBatch || num_qo_heads > kNoAllocMaxHeads || num_qo_heads * head_dim > kNoAllocMaxHeadsDim) {
     set_last_message("nqt_decode_attention_noalloc: shape beyond the fixed scratch (batch <= 1024, "
