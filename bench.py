@@ -52,6 +52,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=300)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--workload", choices=("decode", "mixed"), default="decode",
+                   help="decode = BASELINE config 2 (the headline); mixed = config 4 (prefill chunks + decode rows)")
     p.add_argument("--layers", type=int, default=28, help="decoder layers (28 = BASELINE config 2)")
     p.add_argument("--pool-tokens", type=int, default=POOL_TOKENS)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
@@ -225,11 +227,140 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def peak_tflops() -> float:
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        return float(json.loads(f.read_text())["bf16_tflops"])
+    return 1590.0
+
+
+def time_graph(fn, reps: int, stream) -> float:
+    """ms per replay of a graph of fn() (after warm replays)."""
+
+    fn()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    a1.record(stream)
+    torch.cuda.synchronize()
+    return a0.elapsed_time(a1) / reps
+
+
+def run_mixed(args, world, rank, local) -> None:
+    """8 chunked prefills U[128, 1024] + 240 decode rows ctx U[32, 4096], GPU planner each
+    step, 10 % of the sequences finish and are replaced each step (on the device)."""
+
+    from importlib import import_module
+
+    nqt = import_module("nari-qwen3-tts_b200")
+    talker_step = import_module("nari-qwen3-tts_b200.talker_step")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = torch.Generator().manual_seed(2000 + rank)
+    chunks = torch.randint(128, 1025, (8,), generator=g).tolist()
+    decode_ctx = torch.randint(32, 4097, (240,), generator=g).tolist()
+    shape = talker_step.TalkerShape(num_layers=args.layers)
+    pool_tokens = max(args.pool_tokens, sum(decode_ctx) + sum(chunks) + 64 * 1024)
+    step = talker_step.TalkerMixedStep(shape=shape, chunks=chunks, decode_contexts=decode_ctx, churn_rows=24,
+                                       total_pages=pool_tokens // 16, page_size=16, device=dev, seed=rank)
+    step.admit(scatter_seed=rank)
+    step.capture(warmup=2)
+    for _ in range(args.warmup):
+        step.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            step.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world) / args.steps
+    tokens = step.tokens
+    # prefill attention (tcgen05) alone over the step's metadata, all layers
+    q = torch.randn(tokens, shape.num_heads, shape.head_dim, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    pb, db = step.pre_b, step.dec_b
+
+    def prefill_pass():
+        for layer in range(shape.num_layers):
+            nqt.batch_prefill_paged(q[: step.t_pre], step.storage[layer], pb.qo_indptr, pb.paged_kv_indptr,
+                                    pb.paged_kv_indices, pb.paged_kv_last_page_len, batch=step.n_pre,
+                                    out=out[: step.t_pre])
+
+    def decode_pass():
+        for layer in range(shape.num_layers):
+            nqt.batch_decode_paged(q[step.t_pre:], step.storage[layer], db.paged_kv_indptr, db.paged_kv_indices,
+                                   db.paged_kv_last_page_len, db.decode_workspace, batch_capacity=step.n_dec,
+                                   out=out[step.t_pre:], plan=False)
+
+    reps = 10
+    pre_ms = time_graph(prefill_pass, reps, stream) / shape.num_layers
+    dec_ms = time_graph(decode_pass, reps, stream) / shape.num_layers
+    tflops = step.prefill_flops_per_layer() / (pre_ms / 1e3) / 1e12
+    dec_gbs = step.decode_bytes_per_layer() / (dec_ms / 1e3) / 1e9
+    hbm, _ = peaks()
+    status = nqt.kernels.read_status(dev) | int(step.dec.status.item())
+    line = {
+        "metric": "mixed continuous batch tokens/s (8 prefill chunks + 240 decode rows)",
+        "value": world * tokens / (ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init bf16 weights, N(0,1) KV, seeded chunk and context lengths)",
+        "config": {
+            "workload": f"BASELINE config 4: {shape.num_layers}-layer talker, prefill chunks {chunks} "
+                        f"(sum {step.t_pre}), 240 decode rows ctx U[32,4096] (sum {sum(decode_ctx)}), "
+                        "24 requests replaced per step on the device, GPU planner, CUDA graph",
+            "global_batch": world * step.rows,
+            "seq_len": 4096,
+            "parallelism": f"dp{world} (request-sharded, no collective)",
+            "l2": "inputs larger than L2: ~57 GB of decode KV read per step",
+        },
+        "decode_seq_steps_per_s": world * step.n_dec / (ms / 1e3),
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak_tflops(), "unit": "TFLOP/s",
+                     "frac": tflops / peak_tflops(), "traffic": None,
+                     "kernel": "prefill_tc_kernel (tcgen05 causal prefill)", "flop_per_launch":
+                     step.prefill_flops_per_layer(), "us_per_launch": pre_ms * 1e3,
+                     "peak_source": "measured cuBLAS bf16 burst (MEASURED_PEAKS.json bf16_tflops)"},
+        "decode_roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": hbm, "unit": "GB/s", "frac": dec_gbs / hbm,
+                            "us_per_launch": dec_ms * 1e3, "bytes_per_launch": step.decode_bytes_per_layer()},
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main() -> None:
     args = parse()
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.workload == "mixed":
+        run_mixed(args, world, rank, local)
         return
     nqt = importlib.import_module("nari-qwen3-tts_b200")
     from importlib import import_module

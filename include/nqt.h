@@ -296,7 +296,10 @@ int nqt_planner_init(void* state, int total_pages, int slots, int max_pages_per_
  * When the pool cannot cover the step, NQT_DEV_KV_EXHAUSTED is set and no
  * page is reserved, like KVAllocationError (executor/cache.py:155-158).
  * If `decode_workspace` is not NULL the split-KV plan of nqt_decode_plan is
- * built in the same launch.
+ * built in the same call.  With position_ids, write_pages and write_offsets
+ * all NULL the step only reserves pages and writes the row-level metadata
+ * (admitting a request whose KV is filled elsewhere); token_capacity is then
+ * ignored.
  */
 int nqt_plan_step(
     void* state, int total_pages, int slots, int max_pages_per_slot, int page_size,

@@ -144,13 +144,14 @@ __device__ __forceinline__ int find_seq(const int32_t* tile_indptr, int batch, i
 }
 
 constexpr int kSmemPrefix = 1024;  // tile_indptr entries staged in shared memory (batch + 1 <= this)
+constexpr int kSmemPages = 1024;   // page ids of one CTA's tile range staged in shared memory
 
 template <int D, int HPC, int STAGES>
 struct DecodeCfg {
   static constexpr int kHalves = D / 64;
   static constexpr int kStageBytes = HPC * kHalves * kBoxBytes;
   static constexpr int kThreads = (HPC + 1) * 32;
-  static constexpr int kSmem = STAGES * kStageBytes + 1024 + 2 * STAGES * 8 + 4 * kSmemPrefix;
+  static constexpr int kSmem = STAGES * kStageBytes + 1024 + 2 * STAGES * 8 + 4 * kSmemPrefix + 4 * kSmemPages;
 };
 
 template <int D, int HPC, int STAGES>
@@ -163,6 +164,7 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::kStageBytes);
   uint64_t* empty = full + STAGES;
   int32_t* s_prefix = reinterpret_cast<int32_t*>(empty + STAGES);
+  int32_t* s_pages = s_prefix + kSmemPrefix;
 
   const int c = blockIdx.x;
   const int kv0 = blockIdx.y * HPC;
@@ -192,37 +194,50 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
 
   if (warp == HPC) {
     // ---------------------------------------------------------- producer
-    if (lane == 0) {
-      prefetch_tensormap(&tmap);
-      int seq = find_seq(prefix, p.batch, t_begin);
-      int seq_t0 = prefix[seq];
-      int seq_t1 = prefix[seq + 1];
-      for (int i = 0; i < n_tiles; ++i) {
-        const int64_t t = t_begin + i;
-        while (t >= seq_t1) {  // advance to the owning sequence (skips empty rows)
-          ++seq;
-          seq_t0 = seq_t1;
-          seq_t1 = prefix[seq + 1];
-        }
-        const int s = i % STAGES;
-        if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, p.status)) break;
-        const int in_seq = static_cast<int>(t - seq_t0);
-        const int page_local = in_seq / tpp;
-        const int tile_in_page = in_seq - page_local * tpp;
-        int page = p.indices[p.indptr[seq] + page_local];
-        if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.total_pages)) {
-          report(p.status, NQT_DEV_BAD_PAGE);
-          page = p.total_pages;  // a box entirely outside the map: TMA fills zeros
-        }
-        mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-        uint8_t* dst = smem + s * Cfg::kStageBytes;
-#pragma unroll
-        for (int h = 0; h < HPC; ++h)
-#pragma unroll
-          for (int half = 0; half < kHalves; ++half)
-            tma_load_4d(dst + (h * kHalves + half) * kBoxBytes, &tmap, &full[s], half * 64, kv0 + h,
-                        tile_in_page * kTok, page * 2);
+    // The range's tiles cover one contiguous window of kv_indices (sequences in order, pages in
+    // order): load it once with all 32 lanes so the TMA issue loop never waits on a page-id load.
+    const int seq_a = find_seq(prefix, p.batch, t_begin);
+    const int seq_b = find_seq(prefix, p.batch, t_end - 1);
+    const int win0 = p.indptr[seq_a] + static_cast<int>(t_begin - prefix[seq_a]) / tpp;
+    const int win1 = p.indptr[seq_b] + static_cast<int>(t_end - 1 - prefix[seq_b]) / tpp + 1;
+    const bool windowed = win1 - win0 <= kSmemPages;
+    if (windowed)
+      for (int i = lane; i < win1 - win0; i += 32) s_pages[i] = p.indices[win0 + i];
+    __syncwarp();
+    if (lane == 0) prefetch_tensormap(&tmap);
+    // Lane l issues box l of each stage (KV head l / kHalves, dims half l % kHalves): one thread
+    // issuing every box serialises on the per-instruction TMA issue cost.
+    const int box_h = lane / kHalves, box_half = lane % kHalves;
+    int seq = seq_a;
+    int seq_t0 = prefix[seq];
+    int seq_t1 = prefix[seq + 1];
+    int seq_base = p.indptr[seq];
+    for (int i = 0; i < n_tiles; ++i) {
+      const int64_t t = t_begin + i;
+      while (t >= seq_t1) {  // advance to the owning sequence (skips empty rows)
+        ++seq;
+        seq_t0 = seq_t1;
+        seq_t1 = prefix[seq + 1];
+        seq_base = p.indptr[seq];
       }
+      const int s = i % STAGES;
+      // warp-uniform decision: every lane reaches the same __syncwarp
+      const bool ready = i < STAGES || mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, p.status);
+      if (!__all_sync(kFull, ready)) break;
+      const int in_seq = static_cast<int>(t - seq_t0);
+      const int page_local = in_seq / tpp;
+      const int tile_in_page = in_seq - page_local * tpp;
+      const int pos = seq_base + page_local;
+      int page = windowed ? s_pages[pos - win0] : p.indices[pos];
+      if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.total_pages)) {
+        if (lane == 0) report(p.status, NQT_DEV_BAD_PAGE);
+        page = p.total_pages;  // a box entirely outside the map: TMA fills zeros
+      }
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+      __syncwarp();
+      if (lane < HPC * kHalves)
+        tma_load_4d(smem + s * Cfg::kStageBytes + (box_h * kHalves + box_half) * kBoxBytes, &tmap, &full[s],
+                    box_half * 64, kv0 + box_h, tile_in_page * kTok, page * 2);
     }
     return;
   }

@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_step_kernel(PlanArgs a) {
         if (tm > free_count) {
           report(a.status, NQT_DEV_KV_EXHAUSTED);
           s_fail = 1;
-        } else if (tkv > a.kv_capacity || tt > a.token_capacity) {
+        } else if (tkv > a.kv_capacity || (a.positions != nullptr && tt > a.token_capacity)) {
           report(a.status, NQT_DEV_CAPACITY);
           s_fail = 1;
         }
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_step_kernel(PlanArgs a) {
       const int L = s_len[row];
       const int tp = s_tpref[row];
       const int ps = a.st.pos_start[s];
-      for (int i = lane; i < s_adv[row]; i += 32) {
+      for (int i = lane; a.positions != nullptr && i < s_adv[row]; i += 32) {
         const int abs = L + i;
         const int pi = abs / P;
         const int page = pi < own ? tab[pi] : a.pending[row * pstride + 1 + (pi - own)];
@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_step_kernel(PlanArgs a) {
       int sp = -1;
       if (row < a.scratch_count) sp = a.scratch[row]; else report(a.status, NQT_DEV_CAPACITY);
       if (kvp < a.kv_capacity) a.kv_indices[kvp] = sp < 0 ? 0 : sp;
-      if (!a.prefill) {
+      if (!a.prefill && a.positions != nullptr) {
         const int tp = s_tpref[row];
         if (tp < a.token_capacity) {
           a.write_pages[tp] = sp < 0 ? 0 : sp;
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_step_kernel(PlanArgs a) {
   }
   // spare token slots on the scratch pages
   const int real_tokens = s_real_tokens;
-  for (int t = s_tpref[rows] + tid; t < a.token_capacity; t += kPlanThreads) {
+  for (int t = s_tpref[rows] + tid; a.positions != nullptr && t < a.token_capacity; t += kPlanThreads) {
     const int slot_i = t - real_tokens;
     const int sp_idx = slot_i / P;
     int sp = 0;
@@ -429,10 +429,16 @@ extern "C" int nqt_plan_step(void* state, int total_pages, int slots, int max_pa
                              size_t decode_workspace_bytes, int num_qo_heads, int head_dim, int32_t* status,
                              void* stream) {
   if (!state || !row_slot || !row_advance || !scratch_pages || !kv_indptr || !kv_indices || !last_page_len ||
-      !position_ids || !write_pages || !write_offsets || !pending)
+      !pending)
     return NQT_ERR_ARG;
-  if (prefill && !qo_indptr) return NQT_ERR_ARG;
-  if (capture_rows < 1 || capture_rows > kMaxRows || token_capacity < 1 || page_size < 1) return NQT_ERR_ARG;
+  // allocation-only step: no per-token metadata at all
+  const bool tokens_out = position_ids != nullptr;
+  if (tokens_out != (write_pages != nullptr) || tokens_out != (write_offsets != nullptr)) return NQT_ERR_ARG;
+  if (!tokens_out) token_capacity = 0;
+  if (prefill && tokens_out && !qo_indptr) return NQT_ERR_ARG;
+
+  if (capture_rows < 1 || capture_rows > kMaxRows || (tokens_out && token_capacity < 1) || page_size < 1)
+    return NQT_ERR_ARG;
   if (total_pages < 1 || slots < 1 || max_pages_per_slot < 1 || scratch_count < 0) return NQT_ERR_ARG;
   const int W = (total_pages + 31) / 32;
   if (W > kMaxWordsSmem) return NQT_ERR_UNSUPPORTED;
@@ -449,7 +455,7 @@ extern "C" int nqt_plan_step(void* state, int total_pages, int slots, int max_pa
   a.scratch = scratch_pages;
   a.scratch_count = scratch_count;
   a.prefill = prefill;
-  a.qo_indptr = prefill ? qo_indptr : nullptr;
+  a.qo_indptr = prefill ? qo_indptr : nullptr;  // may be NULL for an allocation-only step
   a.kv_indptr = kv_indptr;
   a.kv_indices = kv_indices;
   a.kv_capacity = kv_indices_capacity;

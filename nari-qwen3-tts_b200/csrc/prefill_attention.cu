@@ -327,14 +327,15 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) prefill_kernel(const __
 namespace tcp {
 constexpr int kM = 128;
 constexpr int kN = 64;
-constexpr int kStages = 3;
+constexpr int kStages = 4;
+constexpr int kSmemPages = 1024;  // page ids of the sequence staged in shared memory
 constexpr int kQBytes = kM * 128 * 2;           // [half][128 rows][128 B]
 constexpr int kKVHalf = kN * 128;               // [64 tokens][128 B]
 constexpr int kKVBytes = 4 * kKVHalf;           // K h0, K h1, V h0, V h1
 constexpr int kPBytes = kM * kN * 2;            // [128 rows][128 B]
 constexpr int kThreads = 6 * 32;
 constexpr int kBarBytes = 256;
-constexpr int kSmem = 1024 + kQBytes + kStages * kKVBytes + 2 * kPBytes + kBarBytes;
+constexpr int kSmem = 1024 + kQBytes + kStages * kKVBytes + 2 * kPBytes + kBarBytes + 4 * kSmemPages;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColO = 128;
 }  // namespace tcp
@@ -358,6 +359,7 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   uint64_t* o_done = p_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   int* info = reinterpret_cast<int*>(tmem_slot + 1);
+  int32_t* s_pages = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -419,38 +421,45 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   if (nb > 0) {
     if (warp == 0) {
       // ------------------------------------------------------------ producer
+      // stage the page ids this tile reads in shared memory (one coalesced pass by the warp)
+      const int32_t* pages_g = p.indices + p.kv_indptr[seq];
+      const int n_used = min(n_pages, (nb * kN + p.page_size - 1) / p.page_size);
+      const bool staged = n_used <= kSmemPages;
+      if (staged)
+        for (int i = lane; i < n_used; i += 32) s_pages[i] = pages_g[i];
+      __syncwarp();
+      const int32_t* pages = staged ? s_pages : pages_g;
       if (lane == 0) {
         prefetch_tensormap(&qmap);
         prefetch_tensormap(&kvmap);
         mbar_arrive_expect_tx(q_full, kQBytes);
         for (int half = 0; half < 2; ++half)
           tma_load_3d(sQ + half * (kQBytes / 2), &qmap, q_full, half * 64, kvh * G, q0 + t_first);
-        const int32_t* pages = p.indices + p.kv_indptr[seq];
-        for (int j = 0; j < nb; ++j) {
-          const int s = j % kStages;
-          if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.status)) break;
-          mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
-          uint8_t* st = sKV + s * kKVBytes;
-#pragma unroll
-          for (int sub = 0; sub < kN / 16; ++sub) {
-            const int pos = j * kN + sub * 16;
-            const int pi = pos / p.page_size;
-            int page = p.total_pages;  // past the sequence: zero-filled box
-            if (pi < n_pages) {
-              page = pages[pi];
-              if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.total_pages)) {
-                report(p.status, NQT_DEV_BAD_PAGE);
-                page = p.total_pages;
-              }
+      }
+      // Lane l issues box l of each block (sub-tile l/4, K or V, dims half): a single thread
+      // issuing all 16 boxes serialises on the per-instruction TMA issue cost.
+      const int sub = lane >> 2, kind = (lane >> 1) & 1, half = lane & 1;
+      for (int j = 0; j < nb; ++j) {
+        const int s = j % kStages;
+        // warp-uniform decision: every lane reaches the same __syncwarp
+        const bool ready = j < kStages || mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.status);
+        if (!__all_sync(kFull, ready)) break;
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
+        __syncwarp();
+        if (lane < 16) {
+          const int pos = j * kN + sub * 16;
+          const int pi = pos / p.page_size;
+          int page = p.total_pages;  // past the sequence: zero-filled box
+          if (pi < n_pages) {
+            page = pages[pi];
+            if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.total_pages)) {
+              report(p.status, NQT_DEV_BAD_PAGE);
+              page = p.total_pages;
             }
-            const int tip = pos - pi * p.page_size;
-#pragma unroll
-            for (int kind = 0; kind < 2; ++kind)
-#pragma unroll
-              for (int half = 0; half < 2; ++half)
-                tma_load_4d(st + (kind * 2 + half) * kKVHalf + sub * 2048, &kvmap, &kv_full[s], half * 64, kvh, tip,
-                            page * 2 + kind);
           }
+          const int tip = pos - pi * p.page_size;
+          tma_load_4d(sKV + s * kKVBytes + (kind * 2 + half) * kKVHalf + sub * 2048, &kvmap, &kv_full[s], half * 64,
+                      kvh, tip, page * 2 + kind);
         }
       }
     } else if (warp == 1) {
@@ -524,14 +533,26 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[sb]);
         const int base = j * kN;
-        float mx = NEG_INF;
+        // raw scores; the causal / length mask only matters on the diagonal and the last block
+        if (base + kN - 1 > lim || base + kN > kv_len) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const int key = base + c;
-          const float v = (key <= lim && key < kv_len) ? __uint_as_float(sr[c]) * p.scale_log2 : NEG_INF;
-          sr[c] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
+          for (int c = 0; c < 64; ++c) {
+            const int key = base + c;
+            if (key > lim || key >= kv_len) sr[c] = __float_as_uint(NEG_INF);
+          }
         }
+        float mx8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float a = fmaxf(fmaxf(__uint_as_float(sr[e]), __uint_as_float(sr[e + 8])),
+                          fmaxf(__uint_as_float(sr[e + 16]), __uint_as_float(sr[e + 24])));
+          float b = fmaxf(fmaxf(__uint_as_float(sr[e + 32]), __uint_as_float(sr[e + 40])),
+                          fmaxf(__uint_as_float(sr[e + 48]), __uint_as_float(sr[e + 56])));
+          mx8[e] = fmaxf(a, b);
+        }
+        const float mx_raw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float mx = mx_raw * p.scale_log2;  // log2 domain (scale > 0 keeps the order)
         const float m_new = fmaxf(m_used, mx);
         const bool need = (m_used != NEG_INF) && (m_new > m_used + 8.f);
         if (__any_sync(kFull, need)) {
@@ -564,20 +585,20 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
           break;
         }
         uint8_t* prow = sP + sb * kPBytes + row * 128;
-        float rs = 0.f;
+        const float sc = p.scale_log2;
+        const float moff = m_used;
+        float rs8[8];
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
-          uint32_t w[4];
+          float pv[8];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = exp2f(__uint_as_float(sr[c8 * 8 + 2 * e]) - m_used);
-            const float p1 = exp2f(__uint_as_float(sr[c8 * 8 + 2 * e + 1]) - m_used);
-            rs += p0 + p1;
-            w[e] = pack_bf16x2(p0, p1);
-          }
-          *reinterpret_cast<uint4*>(prow + ((c8 ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          for (int e = 0; e < 8; ++e) pv[e] = exp2f(fmaf(__uint_as_float(sr[c8 * 8 + e]), sc, -moff));
+          rs8[c8] = ((pv[0] + pv[1]) + (pv[2] + pv[3])) + ((pv[4] + pv[5]) + (pv[6] + pv[7]));
+          *reinterpret_cast<uint4*>(prow + ((c8 ^ (row & 7)) << 4)) =
+              make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]), pack_bf16x2(pv[4], pv[5]),
+                         pack_bf16x2(pv[6], pv[7]));
         }
-        l += rs;
+        l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         if (base + kN > kv_len) {
           // zero V rows at or past kv_len so 0 * stale never meets a NaN
           const int first_bad = max(0, kv_len - base);

@@ -81,6 +81,25 @@ class DevicePagePlanner:
             call("nqt_planner_init", ptr(self.state), total_pages, slots, max_pages_per_slot,
                  scratch_page_count, _lib.stream_handle(device))
 
+    def view(self, *, capture_rows: int, token_capacity: int) -> "DevicePagePlanner":
+        """Another step shape (rows, token capacity) over the same page pool and
+        request slots, with its own row and pending buffers: e.g. the prefill and
+        the decode half of a mixed batch.  token_capacity 0 = allocation only."""
+
+        if capture_rows > self.scratch_pages.numel():
+            raise ValueError("Talker CUDA Graph rows exceed executor-private scratch pages")
+        if token_capacity > self.scratch_pages.numel() * self.page_size:
+            raise ValueError("Talker token capacity exceeds executor-private scratch slots")
+        other = object.__new__(DevicePagePlanner)
+        other.__dict__.update(self.__dict__)
+        other.capture_rows = capture_rows
+        other.token_capacity = token_capacity
+        other.row_slot = torch.full((capture_rows,), -1, dtype=torch.int32, device=self.device)
+        other.row_advance = torch.zeros(capture_rows, dtype=torch.int32, device=self.device)
+        other.row_publish = torch.ones(capture_rows, dtype=torch.int32, device=self.device)
+        other.pending = torch.zeros((capture_rows, self.max_pages + 1), dtype=torch.int32, device=self.device)
+        return other
+
     # -- request bookkeeping (host) -------------------------------------------------
     def add_request(self, request_id: str) -> int:
         if not isinstance(request_id, str) or not request_id:
@@ -105,6 +124,13 @@ class DevicePagePlanner:
         del self._slot_of[request_id]
         self._free_slots.append(slot)
         self._free_slots.sort()
+
+    def release_rows(self) -> None:
+        """Release every page of the slots in ``row_slot`` (device list, graph-capturable)."""
+
+        with torch.cuda.device(self.device):
+            call("nqt_plan_release", ptr(self.state), self.total_pages, self.slots, self.max_pages,
+                 ptr(self.row_slot), self.capture_rows, ptr(self.status), _lib.stream_handle(self.device))
 
     def release(self, slots: list[int]) -> None:
         if not slots:
@@ -162,13 +188,14 @@ class DevicePagePlanner:
 
     def plan_into(self, *, qo_indptr, kv_indptr, kv_indices, last_page_len, position_ids, write_pages,
                   write_offsets, prefill: bool, decode_workspace: torch.Tensor | None = None) -> None:
-        """Same as ``plan`` with explicit output buffers."""
+        """Same as ``plan`` with explicit output buffers (token buffers None:
+        allocation only)."""
 
         with torch.cuda.device(self.device):
             call(
                 "nqt_plan_step",
                 ptr(self.state), self.total_pages, self.slots, self.max_pages, self.page_size,
-                ptr(self.row_slot), ptr(self.row_advance), self.capture_rows, self.token_capacity,
+                ptr(self.row_slot), ptr(self.row_advance), self.capture_rows, max(self.token_capacity, 1),
                 ptr(self.scratch_pages), self.scratch_pages.numel(), 1 if prefill else 0,
                 ptr(qo_indptr), ptr(kv_indptr), ptr(kv_indices), kv_indices.numel(),
                 ptr(last_page_len), ptr(position_ids), ptr(write_pages), ptr(write_offsets), ptr(self.pending),

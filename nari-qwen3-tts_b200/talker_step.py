@@ -33,7 +33,7 @@ import torch.nn.functional as F
 from . import kernels
 from .planner import DevicePagePlanner
 from .sampling import sample_rows
-from .talker_kv import B200TalkerBinding
+from .talker_kv import B200TalkerBinding, batch_decode_paged, batch_prefill_paged
 
 FRAME_OFFSET_STRIDE = 512  # contract/rng.py: 16 codebooks x 32
 
@@ -66,6 +66,59 @@ class _AttentionParams:
         self.rope_theta = theta
 
 
+class TalkerWeights:
+    """Random-init bf16 weights of the talker decoder (the shapes of
+    model/components.py:60-90 and model/layers.py:273-294)."""
+
+    def __init__(self, shape: TalkerShape, device: torch.device, generator: torch.Generator) -> None:
+        s, g, dev, bf16 = shape, generator, device, torch.bfloat16
+
+        def w(out_f, in_f):
+            return (torch.randn(out_f, in_f, generator=g, device=dev) * in_f**-0.5).to(bf16)
+
+        def norm_w(n):
+            return (1.0 + 0.05 * torch.randn(n, generator=g, device=dev)).to(bf16)
+
+        qkv_out = (s.num_heads + 2 * s.num_kv_heads) * s.head_dim
+        self.w_qkv = [w(qkv_out, s.hidden) for _ in range(s.num_layers)]
+        self.w_o = [w(s.hidden, s.num_heads * s.head_dim) for _ in range(s.num_layers)]
+        self.w_gate_up = [w(2 * s.ffn, s.hidden) for _ in range(s.num_layers)]
+        self.w_down = [w(s.hidden, s.ffn) for _ in range(s.num_layers)]
+        self.ln_in = [norm_w(s.hidden) for _ in range(s.num_layers)]
+        self.ln_post = [norm_w(s.hidden) for _ in range(s.num_layers)]
+        self.ln_final = norm_w(s.hidden)
+        self.w_head = w(s.vocab, s.hidden)
+        self.attn = [_AttentionParams(norm_w(s.head_dim), norm_w(s.head_dim), s.eps, s.rope_theta)
+                     for _ in range(s.num_layers)]
+
+    def bytes(self) -> int:
+        tensors = [*self.w_qkv, *self.w_o, *self.w_gate_up, *self.w_down, self.w_head]
+        return sum(t.numel() * t.element_size() for t in tensors)
+
+
+def _kv_pool(shape: TalkerShape, total_pages: int, page_size: int, device, generator) -> torch.Tensor:
+    """Paged KV pool [layers, pages, 2, P, Hkv, D] filled with N(0, 1) data."""
+
+    storage = torch.empty((shape.num_layers, total_pages, 2, page_size, shape.num_kv_heads, shape.head_dim),
+                          dtype=torch.bfloat16, device=device)
+    for layer in range(shape.num_layers):
+        storage[layer].normal_(generator=generator)
+    return storage
+
+
+def _mlp_block(weights: TalkerWeights, shape: TalkerShape, layer: int, o: torch.Tensor, residual: torch.Tensor,
+               act: torch.Tensor) -> torch.Tensor:
+    """residual += o; MLP(norm(residual)); residual += mlp; returns the next layer's normed input."""
+
+    kernels.fused_add_rmsnorm_(o, residual, weights.ln_post[layer], shape.eps)
+    gate_up = F.linear(o, weights.w_gate_up[layer])
+    kernels.silu_and_mul(gate_up, out=act)
+    m = F.linear(act, weights.w_down[layer])
+    nxt = weights.ln_final if layer + 1 == shape.num_layers else weights.ln_in[layer + 1]
+    kernels.fused_add_rmsnorm_(m, residual, nxt, shape.eps)
+    return m
+
+
 class TalkerDecodeStep:
     def __init__(
         self,
@@ -88,30 +141,8 @@ class TalkerDecodeStep:
         self.device = dev = torch.device(device)
         g = torch.Generator(device=dev).manual_seed(seed)
         bf16 = torch.bfloat16
-
-        def w(out_f, in_f):
-            return (torch.randn(out_f, in_f, generator=g, device=dev) * in_f**-0.5).to(bf16)
-
-        def norm_w(n):
-            return (1.0 + 0.05 * torch.randn(n, generator=g, device=dev)).to(bf16)
-
-        qkv_out = (s.num_heads + 2 * s.num_kv_heads) * s.head_dim
-        self.w_qkv = [w(qkv_out, s.hidden) for _ in range(s.num_layers)]
-        self.w_o = [w(s.hidden, s.num_heads * s.head_dim) for _ in range(s.num_layers)]
-        self.w_gate_up = [w(2 * s.ffn, s.hidden) for _ in range(s.num_layers)]
-        self.w_down = [w(s.hidden, s.ffn) for _ in range(s.num_layers)]
-        self.ln_in = [norm_w(s.hidden) for _ in range(s.num_layers)]
-        self.ln_post = [norm_w(s.hidden) for _ in range(s.num_layers)]
-        self.ln_final = norm_w(s.hidden)
-        self.w_head = w(s.vocab, s.hidden)
-        self.attn = [_AttentionParams(norm_w(s.head_dim), norm_w(s.head_dim), s.eps, s.rope_theta)
-                     for _ in range(s.num_layers)]
-
-        # paged KV pool [layers, pages, 2, P, Hkv, D], filled with N(0, 1) data
-        self.storage = torch.empty((s.num_layers, total_pages, 2, page_size, s.num_kv_heads, s.head_dim),
-                                   dtype=bf16, device=dev)
-        for layer in range(s.num_layers):
-            self.storage[layer].normal_(generator=g)
+        self.weights = TalkerWeights(s, dev, g)
+        self.storage = _kv_pool(s, total_pages, page_size, dev, g)
         self.planner = DevicePagePlanner(total_pages=total_pages, page_size=page_size, slots=batch,
                                          max_pages_per_slot=max_pages_per_seq, scratch_page_count=batch,
                                          capture_rows=batch, token_capacity=batch, device=dev,
@@ -170,26 +201,21 @@ class TalkerDecodeStep:
         b = self.binding
         self.planner.plan(b, prefill=False)
         x, residual = self._x, self._residual
+        w = self.weights
         residual.copy_(self.hidden_in)
-        kernels.rmsnorm(self.hidden_in, self.ln_in[0], s.eps, out=x)
+        kernels.rmsnorm(self.hidden_in, w.ln_in[0], s.eps, out=x)
         hq, hkv, d = s.num_heads, s.num_kv_heads, s.head_dim
         rows = self.batch
         for layer in range(s.num_layers):
             b.select_layer(layer)
-            qkv = F.linear(x, self.w_qkv[layer])
+            qkv = F.linear(x, w.w_qkv[layer])
             q = qkv[:, : hq * d].view(rows, hq, d)
             k = qkv[:, hq * d: (hq + hkv) * d].view(rows, hkv, d)
             v = qkv[:, (hq + hkv) * d:].view(rows, hkv, d)
-            attn = b.attend(self.attn[layer], q, k, v)
-            o = F.linear(attn.view(rows, hq * d), self.w_o[layer])
-            kernels.fused_add_rmsnorm_(o, residual, self.ln_post[layer], s.eps)
-            gate_up = F.linear(o, self.w_gate_up[layer])
-            kernels.silu_and_mul(gate_up, out=self._act)
-            m = F.linear(self._act, self.w_down[layer])
-            nxt = self.ln_final if layer + 1 == s.num_layers else self.ln_in[layer + 1]
-            kernels.fused_add_rmsnorm_(m, residual, nxt, s.eps)
-            x = m
-        logits = F.linear(x, self.w_head)
+            attn = b.attend(w.attn[layer], q, k, v)
+            o = F.linear(attn.view(rows, hq * d), w.w_o[layer])
+            x = _mlp_block(w, s, layer, o, residual, self._act)
+        logits = F.linear(x, w.w_head)
         sample_rows(logits, self.temperature, self.top_k, self.top_p, self.seed, self.offset,
                     repetition_penalty=self.penalty, seen_token_mask=self.seen, update_seen=True,
                     round_scaled_to_input=False, out=self.tokens)
@@ -237,8 +263,174 @@ class TalkerDecodeStep:
         return kv + qo
 
     def weight_bytes(self) -> int:
-        tensors = [*self.w_qkv, *self.w_o, *self.w_gate_up, *self.w_down, self.w_head]
-        return sum(t.numel() * t.element_size() for t in tensors)
+        return self.weights.bytes()
 
 
-__all__ = ["TalkerDecodeStep", "TalkerShape"]
+class TalkerMixedStep:
+    """One step of a mixed continuous batch: chunked
+    prefills and decode rows in the same step, one CUDA graph.
+
+    Rows [0, n_prefill) are prefill chunks (their tokens first in the packed
+    token order), rows [n_prefill, n_prefill + n_decode) decode one token each.
+    Each step: the GPU planner plans both groups (two views of one page pool),
+    every layer runs one QKV GEMM over all tokens, QK-norm/RoPE + KV write for
+    both groups, the tcgen05 causal prefill for the chunks and the split-KV
+    decode for the decode rows, then the shared O projection and MLP; the last
+    token of each chunk and every decode row are sampled.  Then ``churn_rows``
+    decode requests finish and are replaced on the device: their pages are
+    released and new requests of the same lengths are admitted through the
+    planner's allocation path (lowest free pages first).  Reservations of the
+    step itself are discarded, so the workload is stationary.
+    """
+
+    def __init__(self, *, shape: TalkerShape = TalkerShape(), chunks: list[int], decode_contexts: list[int],
+                 churn_rows: int = 24, total_pages: int, page_size: int = 16, device: torch.device | str = "cuda",
+                 seed: int = 0) -> None:
+        self.shape = s = shape
+        self.device = dev = torch.device(device)
+        self.page_size = P = page_size
+        self.chunks = list(chunks)
+        self.decode_contexts = list(decode_contexts)
+        self.n_pre, self.n_dec = len(chunks), len(decode_contexts)
+        self.rows = self.n_pre + self.n_dec
+        self.t_pre = sum(chunks)
+        self.tokens = self.t_pre + self.n_dec
+        self.churn_rows = churn_rows
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.weights = TalkerWeights(s, dev, g)
+        self.storage = _kv_pool(s, total_pages, page_size, dev, g)
+        max_len = max(max(chunks), max(decode_contexts)) + 1
+        # scratch pages: the largest prefill chunk set or the decode rows (executor/build.py:40-54)
+        scratch = max((self.t_pre + P - 1) // P, self.n_dec, churn_rows)
+        self.dec = DevicePagePlanner(total_pages=total_pages, page_size=P, slots=self.rows,
+                                     max_pages_per_slot=(max_len + P - 1) // P + 1, scratch_page_count=scratch,
+                                     capture_rows=self.n_dec, token_capacity=self.n_dec, device=dev,
+                                     num_qo_heads=s.num_heads, head_dim=s.head_dim)
+        self.pre = self.dec.view(capture_rows=self.n_pre, token_capacity=self.t_pre)
+        self.adm = self.dec.view(capture_rows=churn_rows, token_capacity=0)
+        common = dict(storage=self.storage, num_qo_heads=s.num_heads, num_kv_heads=s.num_kv_heads,
+                      head_dim=s.head_dim, page_size=P, total_pages=total_pages, device=dev, dtype=torch.bfloat16)
+        self.pre_b = B200TalkerBinding(capture_batch_size=self.n_pre, token_capacity=self.t_pre, **common)
+        self.dec_b = B200TalkerBinding(capture_batch_size=self.n_dec, token_capacity=self.n_dec, **common)
+        # allocation-only metadata sink of the admission step
+        self._adm_indptr = torch.zeros(churn_rows + 1, dtype=torch.int32, device=dev)
+        self._adm_indices = torch.zeros(total_pages + churn_rows, dtype=torch.int32, device=dev)
+        self._adm_last = torch.zeros(churn_rows, dtype=torch.int32, device=dev)
+        self._churn_base = torch.zeros(1, dtype=torch.long, device=dev)
+        self._churn_range = torch.arange(churn_rows, dtype=torch.long, device=dev)
+        self._replacement_len = torch.tensor(decode_contexts, dtype=torch.int32, device=dev)
+        bf16 = torch.bfloat16
+        self.hidden_in = torch.zeros(self.tokens, s.hidden, dtype=bf16, device=dev)
+        self._x = torch.empty(self.tokens, s.hidden, dtype=bf16, device=dev)
+        self._residual = torch.empty(self.tokens, s.hidden, dtype=bf16, device=dev)
+        self._attn = torch.empty(self.tokens, s.num_heads * s.head_dim, dtype=bf16, device=dev)
+        self._act = torch.empty(self.tokens, s.ffn, dtype=bf16, device=dev)
+        ends = torch.tensor(chunks).cumsum(0) - 1
+        self._sample_rows = torch.cat([ends, self.t_pre + torch.arange(self.n_dec)]).to(dev)
+        n = self.rows
+        self.temperature = torch.full((n,), 0.9, device=dev)
+        self.top_k = torch.full((n,), 50, dtype=torch.int32, device=dev)
+        self.top_p = torch.full((n,), 0.95, device=dev)
+        self.penalty = torch.full((n,), 1.05, device=dev)
+        self.seed = torch.arange(n, dtype=torch.long, device=dev)
+        self.offset = torch.zeros(n, dtype=torch.long, device=dev)
+        self.seen = torch.zeros(n, s.vocab, dtype=torch.bool, device=dev)
+        self.out_tokens = torch.zeros(n, dtype=torch.long, device=dev)
+        self.graph: torch.cuda.CUDAGraph | None = None
+
+    def admit(self, *, scatter_seed: int = 0) -> None:
+        """Prefill rows start empty; decode rows get their contexts on scattered pages."""
+
+        P = self.page_size
+        gen = torch.Generator().manual_seed(scatter_seed)
+        scratch = self.dec.scratch_pages.numel()
+        perm = (torch.randperm(self.dec.total_pages - scratch, generator=gen) + scratch).to(torch.int32)
+        pre_slots = [self.dec.add_request(f"prefill{i}") for i in range(self.n_pre)]
+        dec_slots, pos = [], 0
+        for i, n in enumerate(self.decode_contexts):
+            slot = self.dec.add_request(f"decode{i}")
+            pages = (n + P - 1) // P
+            self.dec.import_pages(slot, perm[pos: pos + pages], n)
+            pos += pages
+            dec_slots.append(slot)
+        self.pre.set_rows(pre_slots, self.chunks)
+        self.dec.set_rows(dec_slots, [1] * self.n_dec)
+        ids = torch.randint(0, self.shape.vocab, (self.rows, 64), generator=gen)
+        self.seen.zero_()
+        self.seen.scatter_(1, ids.to(self.device), True)
+
+    def forward(self) -> torch.Tensor:
+        s, w = self.shape, self.weights
+        hq, hkv, d = s.num_heads, s.num_kv_heads, s.head_dim
+        tp, nd, T = self.t_pre, self.n_dec, self.tokens
+        self.pre.plan(self.pre_b, prefill=True)
+        self.dec.plan(self.dec_b, prefill=False)
+        x, residual = self._x, self._residual
+        residual.copy_(self.hidden_in)
+        kernels.rmsnorm(self.hidden_in, w.ln_in[0], s.eps, out=x)
+        for layer in range(s.num_layers):
+            cache = self.storage[layer]
+            qkv = F.linear(x, w.w_qkv[layer])
+            q = qkv[:, : hq * d].view(T, hq, d)
+            k = qkv[:, hq * d: (hq + hkv) * d].view(T, hkv, d)
+            v = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
+            a = w.attn[layer]
+            for b, lo, hi in ((self.pre_b, 0, tp), (self.dec_b, tp, T)):
+                kernels.paired_qk_norm_rope_paged_cache_(
+                    q[lo:hi], k[lo:hi], v[lo:hi], a.q_norm.weight, a.k_norm.weight, b.position_ids, s.eps,
+                    s.rope_theta, cache, b.write_pages, b.write_offsets)
+            attn = self._attn.view(T, hq, d)
+            batch_prefill_paged(q[:tp], cache, self.pre_b.qo_indptr, self.pre_b.paged_kv_indptr,
+                                self.pre_b.paged_kv_indices, self.pre_b.paged_kv_last_page_len, batch=self.n_pre,
+                                out=attn[:tp])
+            batch_decode_paged(q[tp:], cache, self.dec_b.paged_kv_indptr, self.dec_b.paged_kv_indices,
+                               self.dec_b.paged_kv_last_page_len, self.dec_b.decode_workspace, batch_capacity=nd,
+                               out=attn[tp:], plan=False)
+            o = F.linear(self._attn, w.w_o[layer])
+            x = _mlp_block(w, s, layer, o, residual, self._act)
+        logits = F.linear(x.index_select(0, self._sample_rows), w.w_head)
+        sample_rows(logits, self.temperature, self.top_k, self.top_p, self.seed, self.offset,
+                    repetition_penalty=self.penalty, seen_token_mask=self.seen, update_seen=True,
+                    round_scaled_to_input=False, out=self.out_tokens)
+        self.pre.commit(False)
+        self.dec.commit(False)
+        # churn: churn_rows decode requests finish and new ones of the same lengths are admitted
+        slots = (self._churn_base + self._churn_range) % nd
+        self.adm.row_slot.copy_(slots + self.n_pre)
+        self.adm.row_advance.copy_(self._replacement_len.index_select(0, slots))
+        self.adm.release_rows()
+        self.adm.plan_into(qo_indptr=None, kv_indptr=self._adm_indptr, kv_indices=self._adm_indices,
+                           last_page_len=self._adm_last, position_ids=None, write_pages=None, write_offsets=None,
+                           prefill=True)
+        self.adm.commit(True)
+        self._churn_base.add_(self.churn_rows)
+        self.offset.add_(FRAME_OFFSET_STRIDE)
+        return self.out_tokens
+
+    def capture(self, warmup: int = 2) -> None:
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                self.forward()
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.forward()
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def prefill_flops_per_layer(self) -> int:
+        """Causal prefill FLOPs of one layer: 2 (QK^T, PV) x 2 x Hq x D per visible (query, key) pair."""
+
+        s = self.shape
+        pairs = sum(n * (n + 1) // 2 for n in self.chunks)
+        return 4 * s.num_heads * s.head_dim * pairs
+
+    def decode_bytes_per_layer(self) -> int:
+        s = self.shape
+        return sum(n + 1 for n in self.decode_contexts) * 2 * s.num_kv_heads * s.head_dim * 2
+
+
+__all__ = ["TalkerDecodeStep", "TalkerMixedStep", "TalkerShape", "TalkerWeights"]

@@ -163,3 +163,27 @@ def test_device_planner_exhaustion_reserves_nothing(nqt, cuda):
     pl.commit(True)
     assert pl.request_state("a")[1] == 9 and pl.request_state("b")[1] == 9
     assert int(pl.status.item()) == 0
+
+
+def test_mixed_step_churn_keeps_the_pool_stationary(nqt, cuda):
+    # config-4 mechanics at toy size: prefill chunks + decode rows + device-side request replacement
+    from importlib import import_module
+
+    ts = import_module("nari-qwen3-tts_b200.talker_step")
+    shape = ts.TalkerShape(num_layers=2, hidden=256, ffn=512, vocab=512)
+    ctx = torch.randint(32, 400, (16,), generator=torch.Generator().manual_seed(4)).tolist()
+    step = ts.TalkerMixedStep(shape=shape, chunks=[100, 37, 5], decode_contexts=ctx, churn_rows=4,
+                              total_pages=2048, page_size=16, device=cuda, seed=0)
+    step.admit(scatter_seed=1)
+    free0 = step.dec.free_pages()
+    slot_of = {f"decode{i}": step.dec.slot(f"decode{i}") for i in range(16)}
+    for i in range(6):
+        step.forward()
+        torch.cuda.synchronize()
+        assert int(step.dec.status.item()) == 0 and nqt.kernels.read_status(cuda) == 0
+        assert step.dec.free_pages() == free0
+    for i, n in enumerate(ctx):  # replaced requests come back at the same length
+        pages, length, _ = step.dec.request_state(f"decode{i}")
+        assert length == n and len(pages) == (n + 15) // 16
+    assert torch.isfinite(step._x.float()).all()
+    assert set(slot_of.values()) == {step.dec.slot(f"decode{i}") for i in range(16)}
