@@ -52,7 +52,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=300)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("decode", "mixed"), default="decode",
+    p.add_argument("--workload", choices=("decode", "mixed", "cp"), default="decode",
                    help="decode = BASELINE config 2 (the headline); mixed = config 4 (prefill chunks + decode rows)")
     p.add_argument("--layers", type=int, default=28, help="decoder layers (28 = BASELINE config 2)")
     p.add_argument("--pool-tokens", type=int, default=POOL_TOKENS)
@@ -353,6 +353,149 @@ def run_mixed(args, world, rank, local) -> None:
         dist.destroy_process_group()
 
 
+def run_cp(args, world, rank, local) -> None:
+    """one code-predictor frame (15 residual codebooks, each with its own 2048-way head and
+    sampler call) for B=256 rows, 5-layer decoder, hidden 1024, 16/8 heads, D 64, FFN 3072, top-k 50, T 0.9."""
+
+    from importlib import import_module
+
+    nqt = import_module("nari-qwen3-tts_b200")
+    cp = import_module("nari-qwen3-tts_b200.code_predictor")
+    lib_mod = import_module("nari-qwen3-tts_b200._lib")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    rows = 256
+    frame = cp.CodePredictorFrame(rows=rows, device=dev, seed=rank)
+    s = frame.shape
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    frame.past_hidden.copy_(torch.randn(rows, s.talker_hidden, generator=g, device=dev))
+    frame.layer0_token.copy_(torch.randint(0, s.vocab, (rows,), generator=g, device=dev))
+    frame.set_frame(0)
+    lib_mod.reset_launch_count()
+    frame.capture(warmup=2)
+    launches_per_frame = lib_mod.launch_count() // 3
+    for _ in range(args.warmup):
+        frame.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            frame.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world) / args.steps
+
+    # e2e through CodePredictorFrame.step(): pinned H2D of the talker hidden + layer-0 token, D2H of the codes
+    host_hidden = frame.past_hidden.cpu()
+    host_token = frame.layer0_token.cpu()
+    frame.step(host_hidden, host_token)
+    e2e_steps = max(10, args.steps // 2)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        frame.step(host_hidden, host_token)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e2e_steps
+
+    # the fused CP attention launches of one frame (5 layers x 16 positions), timed alone
+    hq, hkv, d = s.num_heads, s.num_kv_heads, s.head_dim
+    q = torch.randn(rows, hq, d, device=dev).to(torch.bfloat16)
+    k = torch.randn(rows, hkv, d, device=dev).to(torch.bfloat16)
+    v = torch.randn(rows, hkv, d, device=dev).to(torch.bfloat16)
+    cache = torch.randn(s.num_layers, rows, 2, s.groups, hkv, d, device=dev).to(torch.bfloat16)
+
+    def cp_attention_pass():
+        for pos in range(s.groups):
+            for layer in range(s.num_layers):
+                nqt.cp_decode_attention_(q, k, v, frame.q_norm[layer], frame.k_norm[layer], frame.positions[:, pos],
+                                         s.eps, s.rope_theta, cache[layer, :, 0], cache[layer, :, 1], pos)
+
+    launches = s.groups * s.num_layers
+    attn_ms = time_graph(cp_attention_pass, 10, stream) / launches
+    # algorithmic bytes: q, k, v read, out written, K/V row written, cache prefix read (positions 0..pos)
+    row_bytes = hkv * d * 2
+    per_pos = [rows * (2 * hq * d * 2 + 2 * row_bytes + 2 * row_bytes + 2 * (pos + 1) * row_bytes)
+               for pos in range(s.groups)]
+    attn_bytes = sum(per_pos) / s.groups
+    logits = frame.logits[0]
+
+    def sampler_pass():
+        for group in range(s.groups - 1):
+            nqt.sample_rows(logits, frame.temperature, frame.top_k, frame.top_p, frame.seed, frame.offsets[:, group],
+                            round_scaled_to_input=False, out=frame._token)
+
+    sampler_us = time_graph(sampler_pass, 10, stream) / (s.groups - 1) * 1e3
+    peak, peak_kind = peaks()
+    achieved = attn_bytes / (attn_ms / 1e3) / 1e9
+    status = nqt.kernels.read_status(dev)
+    line = {
+        "metric": "code-predictor frames/s (B=256, 15 residual codebooks per frame)",
+        "value": world * rows / (ms / 1e3),
+        "unit": "frames/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init bf16 weights, seeded talker hidden states and layer-0 codes)",
+        "config": {
+            "workload": "BASELINE config 3: code-predictor whole frame, B=256 rows, 5 layers, hidden 1024, "
+                        "16/8 heads, D 64, FFN 3072, 15 x (2048-way head + fused sampler, top-k 50, T 0.9), "
+                        "dense 16-position frame cache, one CUDA graph per frame",
+            "global_batch": world * rows,
+            "seq_len": s.groups,
+            "parallelism": f"dp{world} (request-sharded, no collective)",
+            "l2": "inputs larger than L2: 147 MB of layer weights streamed per depth step, 16 depth steps",
+        },
+        "e2e": {"value": world * rows / (e2e_ms / 1e3), "unit": "frames/s",
+                "h2d_bytes_per_step": frame.h2d_bytes(), "d2h_bytes_per_step": frame.d2h_bytes()},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "cp_decode_kernel (fused QK norm + RoPE + cache write + attention)",
+                     "bytes_per_launch": attn_bytes, "us_per_launch": attn_ms * 1e3,
+                     "peak_source": f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"},
+        "sampler_us_per_launch": sampler_us,
+        "gpu_launches": launches_per_frame * args.steps,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.code_predictor import CpuCodePredictorFrame
+
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        port = CpuCodePredictorFrame.random()
+        sample_rows_cpu = 64
+        port.time_frame(8)
+        times = []
+        t_end = time.perf_counter() + args.cpu_seconds
+        while time.perf_counter() < t_end or not times:
+            times.append(port.time_frame(sample_rows_cpu))
+        per_frame = statistics.mean(times) / sample_rows_cpu
+        line["cpu_baseline"] = {
+            "value": 1.0 / per_frame, "unit": "frames/s", "cores": threads, "kind": "port",
+            "sample": f"{len(times)} whole frames of {sample_rows_cpu} rows through the CPU port "
+                      "(oracle/code_predictor.py: bf16-rounded activations, fp32 math, reference CPU sampler)",
+        }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main() -> None:
     args = parse()
     world, rank, local = dist_setup(args)
@@ -361,6 +504,9 @@ def main() -> None:
         return
     if args.workload == "mixed":
         run_mixed(args, world, rank, local)
+        return
+    if args.workload == "cp":
+        run_cp(args, world, rank, local)
         return
     nqt = importlib.import_module("nari-qwen3-tts_b200")
     from importlib import import_module

@@ -193,3 +193,73 @@ def test_code_predictor_strided_offsets(nqt, cuda):
     col = nqt.sample_code_predictor_cuda_graph(logits, *args, offsets[:, 3])
     dense = nqt.sample_code_predictor_cuda_graph(logits, *args, offsets[:, 3].contiguous())
     assert torch.equal(col, dense)
+
+
+def _shaped_rows(g, rows, vocab):
+    """Tie-free row shapes that stress the small-k candidate search: masked (-inf) vocab, one dominant
+    logit, a tight cluster of 70 near-equal leaders (the refinement level), a plain row, a narrow and a
+    wide spread, a boosted block of 100."""
+
+    logits = torch.randn(rows, vocab, generator=g) * 2.0
+    logits[0::8, : vocab // 3] = float("-inf")
+    logits[1::8, 7] += 60.0
+    logits[2::8, 200:270] = 5.0 + torch.randn(logits[2::8, 200:270].shape, generator=g) * 1e-3
+    logits[4::8] *= 1e-3
+    logits[5::8] *= 40.0
+    logits[6::8, :100] += 9.0
+    return logits
+
+
+@pytest.mark.parametrize("top_k", [1, 2, 17, 50, 63, 64, 65])
+def test_small_k_candidate_search_matches_oracle_on_shaped_rows(nqt, cuda, top_k):
+    g = torch.Generator().manual_seed(300 + top_k)
+    rows, vocab = 64, 2048
+    c = {
+        "logits": _shaped_rows(g, rows, vocab),
+        "temperature": torch.rand(rows, generator=g) * 1.5 + 0.05,
+        "top_k": torch.full((rows,), top_k, dtype=torch.int32),
+        "top_p": torch.where(torch.arange(rows) % 2 == 0, torch.ones(rows), torch.rand(rows, generator=g) * 0.9 + 0.1),
+        "seed": torch.randint(0, 2**62, (rows,), generator=g),
+        "offset": torch.randint(0, 2**40, (rows,), generator=g),
+        "repetition_penalty": None,
+        "seen_token_mask": None,
+    }
+    _check_case(nqt, cuda, c)
+
+
+def test_small_k_path_with_penalty(nqt, cuda):
+    g = torch.Generator().manual_seed(77)
+    rows, vocab = 64, 3072
+    c = {
+        "logits": _shaped_rows(g, rows, vocab),
+        "temperature": torch.full((rows,), 0.9),
+        "top_k": torch.full((rows,), 50, dtype=torch.int32),
+        "top_p": torch.full((rows,), 0.95),
+        "seed": torch.arange(rows),
+        "offset": torch.arange(rows) * 512,
+        "repetition_penalty": torch.full((rows,), 1.05),
+        "seen_token_mask": torch.rand(rows, vocab, generator=g) < 0.02,
+    }
+    _check_case(nqt, cuda, c)
+
+
+@pytest.mark.parametrize("top_k", [20, 64, 65, 300])
+def test_tied_rows_rank_by_value_then_token_id(nqt, cuda, top_k):
+    # flat rows and integer-valued rows: every boundary is a tie, so the top-k set and its order are
+    # fixed by (value desc, token id asc); the kept probabilities are the softmax of those values
+    g = torch.Generator().manual_seed(top_k)
+    rows, vocab = 16, 2048
+    logits = torch.randn(rows, vocab, generator=g).mul(1.5).round()
+    logits[::4] = 0.25
+    temperature = torch.full((rows,), 1.0)
+    tokens, probs, ids = nqt.sample_rows(
+        logits.to(cuda), temperature.to(cuda), torch.full((rows,), top_k, dtype=torch.int32, device=cuda),
+        torch.ones(rows, device=cuda), torch.arange(rows, device=cuda), torch.zeros(rows, dtype=torch.long, device=cuda),
+        return_probs=True)
+    ids, probs = ids.cpu().long(), probs.cpu()
+    for row in range(rows):
+        order = sorted(range(vocab), key=lambda i: (-float(logits[row, i]), i))[:top_k]
+        assert ids[row, :top_k].tolist() == order, row
+        want = torch.softmax(logits[row, order], dim=0)
+        torch.testing.assert_close(probs[row, :top_k], want, atol=PROB_ATOL, rtol=0)
+        assert int(tokens[row]) in order
