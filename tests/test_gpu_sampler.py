@@ -263,3 +263,22 @@ def test_tied_rows_rank_by_value_then_token_id(nqt, cuda, top_k):
         want = torch.softmax(logits[row, order], dim=0)
         torch.testing.assert_close(probs[row, :top_k], want, atol=PROB_ATOL, rtol=0)
         assert int(tokens[row]) in order
+
+
+@pytest.mark.parametrize("rows", [400, 800, 2048])
+def test_warps_per_row_variants_match_oracle(nqt, cuda, rows):
+    # the launch gives a row 8, 4, 2 or 1 warps depending on the batch; each width against the oracle
+    g = torch.Generator().manual_seed(rows)
+    vocab = 2048
+    c = {
+        "logits": _shaped_rows(g, rows, vocab),
+        "temperature": torch.rand(rows, generator=g) * 1.5 + 0.05,
+        "top_k": torch.randint(1, 80, (rows,), generator=g, dtype=torch.int32),
+        "top_p": torch.where(torch.arange(rows) % 2 == 0, torch.ones(rows), torch.rand(rows, generator=g) * 0.9 + 0.1),
+        "seed": torch.randint(0, 2**62, (rows,), generator=g),
+        "offset": torch.randint(0, 2**40, (rows,), generator=g),
+        "repetition_penalty": torch.rand(rows, generator=g) + 0.5,
+        "seen_token_mask": torch.rand(rows, vocab, generator=g) < 0.03,
+    }
+    c["temperature"][::11] = 0.0
+    _check_case(nqt, cuda, c)
