@@ -359,6 +359,37 @@ int nqt_fused_add_rmsnorm(void* x, void* residual, const void* weight, int rows,
 int nqt_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
                      int rows, int d, int dtype, void* stream);
 
+/*
+ * Decoder projection Y[m, n] = X[m, k] . W[n, k]^T (bf16, fp32 accumulate;
+ * nn.Linear weight layout), a weight-streaming tcgen05 GEMM for m <= 256.
+ * Replaces the torch/cuBLAS projections of the decoder layers
+ * (model/layers.py:195-270 and model/components.py:300-356, the CP
+ * small_to_mtp_projection and lm heads at executor/code_predictor.py:221)
+ * and the sm90-only fused gate/up path (executor/optimizations.py:22-47).
+ *
+ * nqt_gemm_pack_weight lays W out once (at load time) as contiguous 16 KB
+ * tiles [n / 128][k / 64][128 rows x 64] in the MMA's 128-byte-swizzled
+ * order; packed holds n * k bf16.  interleave_gate_up = 1 packs a gate_up
+ * weight [gate (n/2 rows) | up (n/2 rows)] as blocks [gate 64 | up 64] for
+ * epilogue 2.
+ *
+ * nqt_gemm_bf16 on a packed weight:
+ *   epilogue 0  Y = bf16(acc)
+ *   epilogue 1  Y = bf16(acc + bias[n])
+ *   epilogue 2  (weight packed with interleave_gate_up) Y[m, f] =
+ *               silu(g) * up, g and up rounded to bf16 (the gate_up GEMM
+ *               followed by nqt_silu_and_mul); Y is [m, n / 2].
+ * n % 128 == 0, k % 64 == 0, n * round_up(m, 4) <= 4 Mi; x and the packed weight 16-byte
+ * aligned, ldx (elements) a multiple of 8.  ctas = size of the persistent
+ * stream-K grid (<= 0: one per SM).  Tiles shared by several CTAs are summed
+ * in a per-device static workspace, so the calls of one device are ordered
+ * on one stream.  Launched with programmatic stream serialization.
+ */
+int nqt_gemm_pack_weight(const void* w, int64_t ldw, int n, int k, int interleave_gate_up, void* packed,
+                         void* stream);
+int nqt_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, void* y, int64_t ldy, const void* bias,
+                  int m, int n, int k, int epilogue, int ctas, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

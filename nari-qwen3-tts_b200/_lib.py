@@ -90,6 +90,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqt_rmsnorm": (I, [P, L, P, P, L, I, I, F, I, P]),
     "nqt_fused_add_rmsnorm": (I, [P, P, P, I, I, F, I, P]),
     "nqt_silu_and_mul": (I, [P, L, P, L, I, I, I, P]),
+    "nqt_gemm_pack_weight": (I, [P, L, I, I, I, P, P]),
+    "nqt_gemm_bf16": (I, [P, L, P, P, L, P, I, I, I, I, I, P, P]),
 }
 
 _lock = threading.Lock()

@@ -289,14 +289,19 @@ def cp_decode_attention_(
 
 
 __all__ = [
+    "PackedWeight",
     "clear_status",
     "cp_decode_attention_",
     "decode_attn_nhd_short_cache",
     "device_status",
     "paired_qk_norm_rope_",
     "paired_qk_norm_rope_dense_cache_",
+    "fused_add_rmsnorm_",
+    "linear",
     "paired_qk_norm_rope_paged_cache_",
     "read_status",
+    "rmsnorm",
+    "silu_and_mul",
 ]
 
 
@@ -335,3 +340,60 @@ def silu_and_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torc
     call("nqt_silu_and_mul", ptr(flat), flat.stride(0), ptr(out), out.stride(0), flat.shape[0], d,
          _lib.dtype_code(gate_up.dtype), _lib.stream_handle(gate_up.device))
     return out.view(*gate_up.shape[:-1], d)
+
+
+GEMM_PLAIN = 0
+GEMM_BIAS = 1
+GEMM_SILU_MUL = 2
+
+
+class PackedWeight:
+    """A weight [n, k] laid out once for nqt_gemm_bf16: contiguous 16 KB
+    tiles in the MMA's swizzled order (``gate_up`` interleaves the two
+    halves of a gate_up weight in 64-row blocks for the silu_mul epilogue)."""
+
+    def __init__(self, weight: torch.Tensor, *, gate_up: bool = False) -> None:
+        if weight.dim() != 2 or weight.dtype != torch.bfloat16 or weight.stride(1) != 1:
+            raise ValueError("pack a bf16 [n, k] weight with unit stride along k")
+        n, k = weight.shape
+        if n % 128 or k % 64 or (gate_up and n % 256):
+            raise ValueError("packed weights need n % 128 == 0 (256 for gate_up) and k % 64 == 0")
+        self.n, self.k, self.gate_up = n, k, gate_up
+        self.data = torch.empty(n * k, dtype=torch.bfloat16, device=weight.device)
+        call("nqt_gemm_pack_weight", ptr(weight), weight.stride(0), n, k, 1 if gate_up else 0, ptr(self.data),
+             _lib.stream_handle(weight.device))
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return (self.n, self.k)
+
+
+def linear(x: torch.Tensor, weight: PackedWeight, bias: torch.Tensor | None = None, *,
+           out: torch.Tensor | None = None, split: int = 0) -> torch.Tensor:
+    # split: CTAs of the stream-K grid (0 = one per SM)
+    """x [m, k] @ W[n, k]^T (+ bias) on the weight-streaming tcgen05 GEMM
+    (the decoder projections, model/layers.py:195-270).  A ``gate_up`` packed
+    weight gives silu(gate) * up, [m, n / 2]."""
+
+    if not isinstance(weight, PackedWeight):
+        raise TypeError("linear takes a PackedWeight")
+    if x.dim() != 2 or x.shape[1] != weight.k:
+        raise ValueError("linear needs x [m, k] matching the weight")
+    if x.dtype != torch.bfloat16:
+        raise TypeError("linear computes in bf16")
+    if x.stride(1) != 1:
+        raise ValueError("linear needs unit stride along k")
+    if weight.gate_up and bias is not None:
+        raise ValueError("the silu_mul epilogue takes no bias")
+    m = x.shape[0]
+    cols = weight.n // 2 if weight.gate_up else weight.n
+    if out is None:
+        out = torch.empty((m, cols), dtype=torch.bfloat16, device=x.device)
+    elif out.shape != (m, cols) or out.dtype != torch.bfloat16 or out.stride(1) != 1:
+        raise ValueError("linear output must be bf16 [m, n] with unit column stride")
+    epilogue = GEMM_SILU_MUL if weight.gate_up else (GEMM_BIAS if bias is not None else GEMM_PLAIN)
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.shape != (weight.n,) or not bias.is_contiguous()):
+        raise ValueError("linear bias must be contiguous bf16 [n]")
+    call("nqt_gemm_bf16", ptr(x), x.stride(0), ptr(weight.data), ptr(out), out.stride(0), ptr(bias),
+         m, weight.n, weight.k, epilogue, int(split), ptr(device_status(x.device)), _lib.stream_handle(x.device))
+    return out
