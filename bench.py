@@ -52,7 +52,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=300)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("decode", "mixed", "cp"), default="decode",
+    p.add_argument("--workload", choices=("decode", "mixed", "cp", "sampler"), default="decode",
                    help="decode = BASELINE config 2 (the headline); mixed = config 4 (prefill chunks + decode rows)")
     p.add_argument("--layers", type=int, default=28, help="decoder layers (28 = BASELINE config 2)")
     p.add_argument("--pool-tokens", type=int, default=POOL_TOKENS)
@@ -496,6 +496,106 @@ def run_cp(args, world, rank, local) -> None:
         dist.destroy_process_group()
 
 
+def run_sampler(args, world, rank, local) -> None:
+    """The fused sampler's HBM roofline: the talker sampling of 256 decode steps of B=64 stacked into one
+    16384-row launch (V 3072, bf16 logits, seen mask with 64 ids per row, penalty 1.05, T 0.9, top-k 50,
+    top-p 0.95).  Two logits/seen buffer sets alternate so consecutive launches miss L2."""
+
+    from importlib import import_module
+
+    nqt = import_module("nari-qwen3-tts_b200")
+    lib_mod = import_module("nari-qwen3-tts_b200._lib")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    rows, vocab = 256 * BATCH, 3072
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    sets = []
+    for _ in range(2):
+        logits = (torch.randn(rows, vocab, generator=g, device=dev) * 2.0).to(torch.bfloat16)
+        seen = torch.zeros(rows, vocab, dtype=torch.bool, device=dev)
+        seen.scatter_(1, torch.randint(0, vocab, (rows, 64), generator=g, device=dev), True)
+        sets.append((logits, seen))
+    temp = torch.full((rows,), 0.9, device=dev)
+    top_k = torch.full((rows,), 50, dtype=torch.int32, device=dev)
+    top_p = torch.full((rows,), 0.95, device=dev)
+    pen = torch.full((rows,), 1.05, device=dev)
+    seed = torch.arange(rows, device=dev)
+    offset = torch.zeros(rows, dtype=torch.long, device=dev)
+    out = torch.empty(rows, dtype=torch.long, device=dev)
+
+    def launch(i):
+        logits, seen = sets[i & 1]
+        nqt.sample_rows(logits, temp, top_k, top_p, seed, offset, repetition_penalty=pen, seen_token_mask=seen,
+                        out=out)
+
+    for i in range(args.warmup):
+        launch(i)
+    torch.cuda.synchronize()
+    lib_mod.reset_launch_count()
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for i in range(args.steps):
+            launch(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    launches = lib_mod.launch_count()
+    ms = max_over_ranks(start.elapsed_time(end), world) / args.steps
+    # algorithmic bytes: logits + seen mask read, tokens written
+    bytes_per = rows * vocab * (2 + 1) + rows * 8
+    achieved = bytes_per / (ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    # e2e: the same launch from pinned host logits (H2D inside the timed region) and tokens read back
+    host_logits = sets[0][0].cpu().pin_memory()
+    host_tokens = torch.empty(rows, dtype=torch.long).pin_memory()
+    e_steps = max(5, args.steps // 4)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        sets[0][0].copy_(host_logits, non_blocking=True)
+        launch(0)
+        host_tokens.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e_steps
+    line = {
+        "metric": "fused sampler rows/s (talker sampling, 16384 stacked rows x V 3072)",
+        "value": world * rows / (ms / 1e3),
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (N(0,2) logits, 64 seen ids per row)",
+        "config": {"workload": "sampler roofline: 256 talker steps x B=64 stacked, V 3072, penalty 1.05, T 0.9, "
+                               "top-k 50, top-p 0.95, Philox draw", "global_batch": world * rows, "seq_len": vocab,
+                   "parallelism": f"dp{world}", "l2": "two 151 MB input sets alternate (> L2)"},
+        "e2e": {"value": world * rows / (e_ms / 1e3), "unit": "rows/s",
+                "h2d_bytes_per_step": host_logits.numel() * 2, "d2h_bytes_per_step": rows * 8},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "sample_kernel", "bytes_per_launch": bytes_per,
+                     "us_per_launch": ms * 1e3, "peak_source": f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "device_status": nqt.kernels.read_status(dev),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main() -> None:
     args = parse()
     world, rank, local = dist_setup(args)
@@ -507,6 +607,9 @@ def main() -> None:
         return
     if args.workload == "cp":
         run_cp(args, world, rank, local)
+        return
+    if args.workload == "sampler":
+        run_sampler(args, world, rank, local)
         return
     nqt = importlib.import_module("nari-qwen3-tts_b200")
     from importlib import import_module
