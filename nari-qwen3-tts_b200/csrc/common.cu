@@ -1,5 +1,6 @@
 // Host-side helpers shared by every entry point: error text, launch checks,
 // SM count, ABI version.
+#include <math.h>
 #include <stdio.h>
 
 #include "common.cuh"
@@ -29,6 +30,11 @@ int num_sms() {
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return 148;
   return sms;
+}
+
+void rope_inv_freq_table(float* out, int head_dim, float rope_theta) {
+  const double ln_theta = log(static_cast<double>(rope_theta));
+  for (int i = 0; i < head_dim / 2; ++i) out[i] = static_cast<float>(exp(-ln_theta * (2.0 * i / head_dim)));
 }
 
 }  // namespace nqt

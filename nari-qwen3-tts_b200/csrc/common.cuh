@@ -29,6 +29,10 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 int num_sms();
 
+// RoPE inverse frequencies theta^(-2i/D) for i < D / 2, evaluated in double and rounded once
+// (exp(-ln(theta) * 2i / D), the reference's formula) into out[0 .. D / 2).
+void rope_inv_freq_table(float* out, int head_dim, float rope_theta);
+
 // ---------------------------------------------------------------- device side
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -168,11 +172,6 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
   return v;
-}
-
-// RoPE inverse frequency theta^(-2i/D), evaluated in double and rounded once.
-__device__ __forceinline__ float rope_inv_freq(int i, int head_dim, float rope_theta) {
-  return static_cast<float>(exp(-log(static_cast<double>(rope_theta)) * (2.0 * i / head_dim)));
 }
 
 }  // namespace nqt

@@ -27,12 +27,13 @@ struct QkArgs {
   int tokens, hq, hkv;
   float eps, theta;
   int32_t* status;
+  float inv_freq[128];  // RoPE theta^(-2i/D), i < D / 2, evaluated on the host
 };
 
 // Normalise + rotate one head vector in place.  Returns nothing; the rotated
 // values are left in first[]/second[] (fp32, before the final rounding).
 template <typename T, int D>
-__device__ __forceinline__ void norm_rope_head(T* base, const T* weight, float pos, float eps, float theta,
+__device__ __forceinline__ void norm_rope_head(T* base, const T* weight, float pos, float eps, const float* inv_freq,
                                                bool round_norm, float (&first)[D / 64], float (&second)[D / 64]) {
   constexpr int J = D / 64;
   constexpr int H = D / 2;
@@ -56,7 +57,7 @@ __device__ __forceinline__ void norm_rope_head(T* base, const T* weight, float p
       a = to_f32(from_f32<T>(a));
       b = to_f32(from_f32<T>(b));
     }
-    const float angle = pos * rope_inv_freq(i, D, theta);
+    const float angle = pos * inv_freq[i];
     float s, c;
     sincosf(angle, &s, &c);
     first[j] = a * c - b * s;
@@ -67,7 +68,7 @@ __device__ __forceinline__ void norm_rope_head(T* base, const T* weight, float p
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(256) qk_norm_rope_paged_kernel(QkArgs a, T* cache, int total_pages,
+__global__ void __launch_bounds__(256) qk_norm_rope_paged_kernel(const __grid_constant__ QkArgs a, T* cache, int total_pages,
                                                                  int page_size, const int64_t* write_pages,
                                                                  const int64_t* write_offsets) {
   const int token = blockIdx.x;
@@ -81,7 +82,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_paged_kernel(QkArgs a, T* ca
   const T* w = static_cast<const T*>(is_q ? a.qw : a.kw);
   const float pos = static_cast<float>(a.pos[token * a.pos_stride]);
   float first[D / 64], second[D / 64];
-  norm_rope_head<T, D>(base, w, pos, a.eps, a.theta, true, first, second);
+  norm_rope_head<T, D>(base, w, pos, a.eps, a.inv_freq, true, first, second);
   if (is_q) return;
   const int64_t page = write_pages[token];
   const int64_t off = write_offsets[token];
@@ -106,7 +107,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_paged_kernel(QkArgs a, T* ca
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(256) qk_norm_rope_dense_kernel(QkArgs a, T* k_cache, T* v_cache,
+__global__ void __launch_bounds__(256) qk_norm_rope_dense_kernel(const __grid_constant__ QkArgs a, T* k_cache, T* v_cache,
                                                                  int64_t c_row, int64_t c_pos, int64_t c_head,
                                                                  int cache_position, int round_norm) {
   const int token = blockIdx.x;
@@ -120,7 +121,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_dense_kernel(QkArgs a, T* k_
   const T* w = static_cast<const T*>(is_q ? a.qw : a.kw);
   const float pos = static_cast<float>(a.pos[token * a.pos_stride]);
   float first[D / 64], second[D / 64];
-  norm_rope_head<T, D>(base, w, pos, a.eps, a.theta, round_norm != 0, first, second);
+  norm_rope_head<T, D>(base, w, pos, a.eps, a.inv_freq, round_norm != 0, first, second);
   if (is_q || k_cache == nullptr) return;
   constexpr int H = D / 2;
   T* kdst = k_cache + token * c_row + static_cast<int64_t>(cache_position) * c_pos + head * c_head;
@@ -192,7 +193,8 @@ extern "C" int nqt_qk_norm_rope_paged_kv_write(
   if (tokens == 0) return NQT_OK;
   if ((num_qo_heads + num_kv_heads + 7) / 8 > 65535) return NQT_ERR_UNSUPPORTED;
   QkArgs a{q, q_stride_tok, q_stride_head, k, k_stride_tok, k_stride_head, v, v_stride_tok, v_stride_head,
-           q_weight, k_weight, position_ids, 1, tokens, num_qo_heads, num_kv_heads, eps, rope_theta, status};
+           q_weight, k_weight, position_ids, 1, tokens, num_qo_heads, num_kv_heads, eps, rope_theta, status, {}};
+  rope_inv_freq_table(a.inv_freq, head_dim, rope_theta);
   cudaStream_t s = as_stream(stream);
   if (dtype == NQT_BF16)
     return launch_paged<__nv_bfloat16>(a, layer_cache, total_pages, page_size, write_pages, write_offsets, head_dim, s);
@@ -216,7 +218,8 @@ extern "C" int nqt_qk_norm_rope_dense(
   if (tokens == 0) return NQT_OK;
   QkArgs a{q, q_stride_tok, q_stride_head, k, k_stride_tok, k_stride_head, v, v_stride_tok, v_stride_head,
            q_weight, k_weight, positions, positions_stride, tokens, num_qo_heads, num_kv_heads, eps, rope_theta,
-           status};
+           status, {}};
+  rope_inv_freq_table(a.inv_freq, head_dim, rope_theta);
   cudaStream_t s = as_stream(stream);
   if (dtype == NQT_BF16)
     return launch_dense<__nv_bfloat16>(a, k_cache, v_cache, cache_stride_row, cache_stride_pos, cache_stride_head,
