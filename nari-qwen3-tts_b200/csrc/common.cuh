@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/nqt.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ != 1000)
@@ -27,6 +29,26 @@ int check_launch(const char* what);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Launch with programmatic stream serialization: the grid may be scheduled
+// while the previous kernel of the stream is still running, and must execute
+// griddepcontrol.wait (grid_dependency_wait) before it reads anything that
+// kernel (or an earlier one) wrote.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 int num_sms();
 
 // RoPE inverse frequencies theta^(-2i/D) for i < D / 2, evaluated in double and rounded once
@@ -39,6 +61,13 @@ constexpr unsigned kFull = 0xffffffffu;
 // Upper bound on any mbarrier wait: 2 s of %globaltimer.  A healthy wait
 // ends in microseconds; after this the kernel records NQT_DEV_TIMEOUT.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// Programmatic dependent launch: wait until the previous grid of the stream has
+// completed and its memory is visible; let the next grid be scheduled early.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;

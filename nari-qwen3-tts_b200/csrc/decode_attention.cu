@@ -166,6 +166,10 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   int32_t* s_prefix = reinterpret_cast<int32_t*>(empty + STAGES);
   int32_t* s_pages = s_prefix + kSmemPrefix;
 
+  // launched with programmatic serialization: the plan and q come from earlier kernels; the merge
+  // kernel may be scheduled as soon as every CTA here has started
+  grid_dependency_wait();
+  grid_dependents_launch();
   const int c = blockIdx.x;
   const int kv0 = blockIdx.y * HPC;
   const int64_t total = p.header[0];
@@ -440,12 +444,22 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
 }
 
 // ------------------------------------------------------------------ merge
-// One CTA per sequence; sequences that one CTA covered whole exit at once.  Thread
-// (head, 4 dims) combines the split partials: out = sum_i w_i O_i / sum_i w_i,
-// w_i = 2^(lse_i - max lse); the loads of up to 16 contributors are issued together.
+// One CTA per sequence; sequences that one CTA covered whole exit at once.
+// The contributing CTAs (slot 2c when the sequence starts inside CTA c's
+// range, 2c + 1 otherwise) are visited in batches of kMergeBatch whose slots
+// and per-head lse are staged in shared memory: pass 1 finds each head's max
+// lse and weight sum, pass 2 accumulates out = sum_i w_i O_i / sum_i w_i,
+// w_i = 2^(lse_i - max lse), thread (head, 4 dims) issuing the loads of a
+// batch before using them.
+constexpr int kMergeBatch = 64;
+constexpr int kMergeHeads = 64;
+
 template <int D>
-__global__ void __launch_bounds__(512) decode_merge_kernel(DecodeArgs p) {
-  constexpr int kBatch = 16;
+__global__ void __launch_bounds__(256) decode_merge_kernel(DecodeArgs p) {
+  __shared__ int s_slot[kMergeBatch];
+  __shared__ float s_w[kMergeBatch * kMergeHeads];  // lse, then the weight, per (contributor, head)
+  __shared__ float s_max[kMergeHeads], s_inv[kMergeHeads];
+  grid_dependency_wait();  // the decode kernel's partials
   const int seq = blockIdx.x;
   const int64_t total = p.header[0];
   const int n = p.n_ctas;
@@ -461,46 +475,99 @@ __global__ void __launch_bounds__(512) decode_merge_kernel(DecodeArgs p) {
   const int c1 = static_cast<int>((tb1 * n + total - 1) / total) - 1;
   if (c0 == c1) return;  // written directly by the decode kernel
   const float NEG_INF = -__int_as_float(0x7f800000);
-  for (int idx = threadIdx.x; idx < p.hq * (D / 4); idx += blockDim.x) {
+  const int hq = p.hq;
+
+  // stage the slots and lse of contributors [cb, cb + nb)
+  auto stage = [&](int cb, int nb) {
+    __syncthreads();
+    if (threadIdx.x < nb) {
+      const int cc = cb + threadIdx.x;
+      const int64_t st = range_start(total, cc, n);
+      s_slot[threadIdx.x] = st != range_start(total, cc + 1, n) ? ((st >= tb0) ? 2 * cc : 2 * cc + 1) : -1;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nb * hq; i += blockDim.x) {
+      const int k = i / hq, h = i % hq;
+      s_w[k * kMergeHeads + h] =
+          s_slot[k] >= 0 ? p.part_lse[static_cast<int64_t>(s_slot[k]) * hq + h] : NEG_INF;
+    }
+    __syncthreads();
+  };
+
+  // pass 1: per head, the max lse and the weight sum relative to it
+  float mx_h = NEG_INF, sum_h = 0.f;
+  for (int cb = c0; cb <= c1; cb += kMergeBatch) {
+    const int nb = min(kMergeBatch, c1 - cb + 1);
+    stage(cb, nb);
+    if (threadIdx.x < hq) {
+      const int h = threadIdx.x;
+      float bm = NEG_INF;
+      for (int k = 0; k < nb; ++k) bm = fmaxf(bm, s_w[k * kMergeHeads + h]);
+      const float nm = fmaxf(mx_h, bm);
+      sum_h *= mx_h == NEG_INF ? 0.f : exp2f(mx_h - nm);
+      mx_h = nm;
+      for (int k = 0; k < nb; ++k) sum_h += s_slot[k] >= 0 ? exp2f(s_w[k * kMergeHeads + h] - nm) : 0.f;
+    }
+  }
+  if (threadIdx.x < hq) {
+    s_max[threadIdx.x] = mx_h;
+    s_inv[threadIdx.x] = 1.f / sum_h;
+  }
+
+  // pass 2: the weighted sum of the partial outputs
+  const int per_thread = (hq * (D / 4) + blockDim.x - 1) / blockDim.x;  // (head, 4 dims) items per thread
+  float4 acc[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int cb = c0; cb <= c1; cb += kMergeBatch) {
+    const int nb = min(kMergeBatch, c1 - cb + 1);
+    if (c1 - c0 + 1 > kMergeBatch) {
+      stage(cb, nb);
+    } else {
+      __syncthreads();  // one batch: pass 1 left its slots and lse staged; s_max is written
+    }
+    for (int i = threadIdx.x; i < nb * hq; i += blockDim.x) {
+      const int k = i / hq, h = i % hq;
+      s_w[k * kMergeHeads + h] = s_slot[k] >= 0 ? exp2f(s_w[k * kMergeHeads + h] - s_max[h]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int idx = threadIdx.x + r * blockDim.x;
+      if (r >= per_thread || idx >= hq * (D / 4)) continue;
+      const int h = idx / (D / 4);
+      const int d = (idx % (D / 4)) * 4;
+      for (int k0 = 0; k0 < nb; k0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int sl = k0 + k < nb ? s_slot[k0 + k] : -1;
+          v[k] = sl >= 0 ? *reinterpret_cast<const float4*>(p.part_o + (static_cast<int64_t>(sl) * hq + h) * D + d)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (k0 + k < nb) {
+            const float w = s_w[(k0 + k) * kMergeHeads + h];
+            acc[r].x += w * v[k].x;
+            acc[r].y += w * v[k].y;
+            acc[r].z += w * v[k].z;
+            acc[r].w += w * v[k].w;
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int idx = threadIdx.x + r * blockDim.x;
+    if (r >= per_thread || idx >= hq * (D / 4)) continue;
     const int h = idx / (D / 4);
     const int d = (idx % (D / 4)) * 4;
-    float mx = NEG_INF, wsum = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int cb = c0; cb <= c1; cb += kBatch) {
-      int slot[kBatch];
-      float lse[kBatch];
-      float4 v[kBatch];
-#pragma unroll
-      for (int k = 0; k < kBatch; ++k) {
-        const int cc = cb + k;
-        slot[k] = -1;
-        if (cc <= c1) {
-          const int64_t st = range_start(total, cc, n);
-          if (st != range_start(total, cc + 1, n)) slot[k] = (st >= tb0) ? 2 * cc : 2 * cc + 1;
-        }
-        const int64_t sl = slot[k] >= 0 ? slot[k] : 0;
-        lse[k] = slot[k] >= 0 ? p.part_lse[sl * p.hq + h] : NEG_INF;
-        v[k] = *reinterpret_cast<const float4*>(p.part_o + (sl * p.hq + h) * D + d);
-      }
-      float bm = NEG_INF;
-#pragma unroll
-      for (int k = 0; k < kBatch; ++k) bm = fmaxf(bm, lse[k]);
-      const float nm = fmaxf(mx, bm);
-      const float sc = mx == NEG_INF ? 0.f : exp2f(mx - nm);
-      wsum *= sc;
-      acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
-#pragma unroll
-      for (int k = 0; k < kBatch; ++k) {
-        const float w = slot[k] >= 0 ? exp2f(lse[k] - nm) : 0.f;
-        wsum += w;
-        acc.x += w * v[k].x; acc.y += w * v[k].y; acc.z += w * v[k].z; acc.w += w * v[k].w;
-      }
-      mx = nm;
-    }
-    const float inv = 1.f / wsum;
+    const float inv = s_inv[h];
     __nv_bfloat16* ob = p.out + seq * p.o_st + static_cast<int64_t>(h) * p.o_sh + d;
-    *reinterpret_cast<__nv_bfloat162*>(ob) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-    *reinterpret_cast<__nv_bfloat162*>(ob + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<__nv_bfloat162*>(ob) = __floats2bfloat162_rn(acc[r].x * inv, acc[r].y * inv);
+    *reinterpret_cast<__nv_bfloat162*>(ob + 2) = __floats2bfloat162_rn(acc[r].z * inv, acc[r].w * inv);
   }
 }
 
@@ -548,11 +615,18 @@ int launch_decode(const CUtensorMap& map, DecodeArgs a, int groups, int max_ctas
   if (n < 1) n = 1;
   if (n > max_ctas) n = max_ctas;
   a.n_ctas = n;
-  decode_kernel<D, HPC, STAGES><<<dim3(n, groups), Cfg::kThreads, Cfg::kSmem, s>>>(map, a);
-  int rc = check_launch("decode_attention");
-  if (rc != NQT_OK) return rc;
-  decode_merge_kernel<D><<<a.batch, 256, 0, s>>>(a);
-  return check_launch("decode_merge");
+  cudaError_t err =
+      launch_pdl(decode_kernel<D, HPC, STAGES>, dim3(n, groups), dim3(Cfg::kThreads), Cfg::kSmem, s, map, a);
+  if (err != cudaSuccess) {
+    set_last_error("decode_attention", err);
+    return NQT_ERR_CUDA;
+  }
+  err = launch_pdl(decode_merge_kernel<D>, dim3(a.batch), dim3(256), 0, s, a);
+  if (err != cudaSuccess) {
+    set_last_error("decode_merge", err);
+    return NQT_ERR_CUDA;
+  }
+  return NQT_OK;
 }
 
 // KV heads per CTA and TMA pipeline depth of the widest configuration (4 heads: 32 KB stages,
@@ -608,6 +682,8 @@ int check_decode_args(const void* q, int64_t q_stride_tok, int64_t q_stride_head
   if (num_kv_heads < 1 || num_qo_heads % num_kv_heads) return NQT_ERR_ARG;
   if (num_qo_heads / num_kv_heads > 8 || num_kv_heads > 256) return NQT_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return NQT_ERR_UNSUPPORTED;
+  // the merge kernel stages per-head weights of kMergeHeads heads and holds <= 4 items per thread
+  if (num_qo_heads > kMergeHeads || num_qo_heads * head_dim / 4 > 4 * 256) return NQT_ERR_UNSUPPORTED;
   if (page_size < kTok || page_size % kTok || page_size > 256) return NQT_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(layer_cache) & 15) || (reinterpret_cast<uintptr_t>(q) & 3)) return NQT_ERR_ARG;
   if ((q_stride_tok & 1) || (q_stride_head & 1)) return NQT_ERR_ARG;
