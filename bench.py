@@ -13,7 +13,7 @@ the data path); timing is the max over ranks (gloo for the scalar reduce).
 Reported on the JSON line besides the throughput:
   e2e          the same metric through TalkerDecodeStep.step() with host
                buffers: pinned H2D of the step inputs, replay, D2H of tokens;
-  roofline     the decode-attention launch (decode + merge kernels) timed
+  roofline     the decode-attention launch (one decode kernel, fused fix-up) timed
                alone with CUDA events over the same metadata: algorithmic
                KV + q + out bytes / duration vs the measured HBM copy peak;
   cpu_baseline the CPU port of the step (oracle/talker_step.py) on a bounded
@@ -732,7 +732,7 @@ def main() -> None:
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
                 "d2h_bytes_per_step": BATCH * 8},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "kernel": "decode attention (decode_kernel + decode_merge_kernel)",
+                     "traffic": traffic, "kernel": "decode attention (decode_kernel, fused split fix-up)",
                      "bytes_per_launch": attn_bytes, "us_per_launch": attn_ms * 1e3,
                      "peak_source": f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"},
         "gpu_launches": launches_per_step * args.steps,

@@ -145,7 +145,7 @@ int nqt_decode_attention(
  * workspace - e.g. a host whose device memory is owned by another runtime's
  * allocator, or a loader that only passes pointers to buffers it already
  * holds.  Its scratch (plan + split partials) is one fixed array inside the
- * library, nqt_decode_noalloc_scratch_bytes() bytes (about 4.8 MB), held on
+ * library, nqt_decode_noalloc_scratch_bytes() bytes (about 5.1 MB), held on
  * every GPU that loads the library until the process exits.
  * Limits: batch <= 1024, num_qo_heads <= 32, num_qo_heads * head_dim <= 2048;
  * larger shapes return NQT_ERR_CAPACITY (see nqt_last_error).

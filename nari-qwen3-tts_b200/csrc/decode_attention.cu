@@ -9,7 +9,10 @@
 // the ragged lengths are.  A sequence covered by one CTA is written
 // straight to `out`; otherwise each covering CTA leaves a normalised
 // partial (O, lse) in slot 2c (its first segment) or 2c+1 (its last) and
-// the merge kernel combines them.  No CTA waits on another.
+// counts itself in on a per-(sequence, KV head) ticket; the consumer warp
+// that arrives last combines the partials of its query heads and writes
+// `out` (stream-K style fix-up), so no second kernel and no grid-wide wait
+// stand between the last tile and the output.  No CTA waits on another.
 //
 // Data path.  The layer view [pages, 2, P, Hkv, D] is described by a 4-D
 // tensor map {D, Hkv, P, pages*2}.  One TMA box {64, 1, 16, 2} brings
@@ -39,19 +42,21 @@ constexpr int kBoxBytes = 4096;    // [kind 2][tok 16][64 dims] bf16
 constexpr int kMaxSplitCtas = 640; // per head group
 constexpr int kHeaderBytes = 256;
 
-__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+__host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct WsLayout {
   size_t tile_indptr;  // i32 [batch_cap + 1]
+  size_t tickets;      // i32 [batch_cap * hq]: arrivals per (sequence, KV head), zero between launches
   size_t part_lse;     // f32 [2 * kMaxSplitCtas * hq]
   size_t part_o;       // f32 [2 * kMaxSplitCtas * hq * D]
   size_t total;
 };
 
-WsLayout ws_layout(int batch_cap, int hq, int d, int max_ctas = kMaxSplitCtas) {
-  WsLayout w;
+constexpr WsLayout ws_layout(int batch_cap, int hq, int d, int max_ctas = kMaxSplitCtas) {
+  WsLayout w{};
   w.tile_indptr = kHeaderBytes;
-  w.part_lse = align_up(w.tile_indptr + 4 * static_cast<size_t>(batch_cap + 1), 256);
+  w.tickets = align_up(w.tile_indptr + 4 * static_cast<size_t>(batch_cap + 1), 256);
+  w.part_lse = align_up(w.tickets + 4 * static_cast<size_t>(batch_cap) * hq, 256);
   w.part_o = align_up(w.part_lse + 4 * static_cast<size_t>(2 * max_ctas) * hq, 256);
   w.total = align_up(w.part_o + 4 * static_cast<size_t>(2 * max_ctas) * hq * d, 256);
   return w;
@@ -67,6 +72,7 @@ struct DecodeArgs {
   const int32_t* last_len;
   const int32_t* tile_indptr;  // workspace
   const int32_t* header;       // workspace: [0] = total tiles
+  int32_t* tickets;            // workspace: [batch][hq], entry b * hq + kv head
   float* part_lse;
   float* part_o;
   int32_t* status;
@@ -76,13 +82,17 @@ struct DecodeArgs {
 
 // ------------------------------------------------------------------ plan
 // Single CTA: tiles_b = (n_pages_b - 1) * P/16 + ceil(last_len_b / 16),
-// exclusive prefix sum into tile_indptr, total into header[0].
+// exclusive prefix sum into tile_indptr, total into header[0]; the fix-up
+// tickets start at zero (the warp that completes a ticket zeroes it again
+// for the next launch on this plan).
 __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* indptr, const int32_t* last_len,
                                                            int batch, int page_size, int32_t* header,
-                                                           int32_t* tile_indptr) {
+                                                           int32_t* tile_indptr, int32_t* tickets,
+                                                           int n_tickets) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry_s;
   const int tpp = page_size / kTok;
+  for (int i = threadIdx.x; i < n_tickets; i += blockDim.x) tickets[i] = 0;
   if (threadIdx.x == 0) carry_s = 0;
   __syncthreads();
   for (int start = 0; start < batch; start += blockDim.x) {
@@ -143,6 +153,89 @@ __device__ __forceinline__ int find_seq(const int32_t* tile_indptr, int batch, i
   return lo;
 }
 
+// CTA owning flat tile t when `total` tiles are split over n CTAs: max c with total * c / n <= t.
+__device__ __forceinline__ int owner_cta(int64_t total, int n, int64_t t) {
+  return static_cast<int>(((t + 1) * n + total - 1) / total) - 1;
+}
+
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int32_t* addr, int32_t v) {
+  int32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
+// Fix-up of one split sequence, run by the consumer warp that completed its ticket: combines the
+// partials of query heads [kvh * G, kvh * G + G) from the covering CTAs c0..c1 and writes them to
+// out.  Contributor i (CTA c0 + i) left its normalised O and its log2-sum-exp in slot 2(c0+i) when
+// the sequence starts inside its range, else 2(c0+i)+1.  out = sum_i w_i O_i / sum_i w_i with
+// w_i = 2^(lse_i - max lse), folded online so one pass over the contributors suffices.  Lane l
+// owns the R float4 columns f = l + 32 r of the group's G * D/4; the partials are read from L2
+// (.cg) in batches of 8 / R contributors, lse and O of a batch issued together.
+template <int D, int R>
+__device__ __forceinline__ void fixup_sequence(const DecodeArgs& p, int seq, int kvh, int64_t total, int n, int c0,
+                                               int c1, int64_t tb0, int lane) {
+  constexpr int QD = D / 4;  // float4 per head
+  constexpr int kPerBatch = 8 / R;
+  const int cols = p.group * QD;  // float4 columns of the group, <= 32 R
+  const int head0 = kvh * p.group;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  float m[R], sum[R];
+  float4 acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    m[r] = NEG_INF;
+    sum[r] = 0.f;
+    acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int cb = c0; cb <= c1; cb += kPerBatch) {
+    float lse[kPerBatch][R];
+    float4 v[kPerBatch][R];
+#pragma unroll
+    for (int k = 0; k < kPerBatch; ++k) {
+      const int cc = cb + k;
+      const int slot = range_start(total, cc, n) >= tb0 ? 2 * cc : 2 * cc + 1;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int f = lane + 32 * r;
+        if (cc <= c1 && f < cols) {
+          const int64_t row = static_cast<int64_t>(slot) * p.hq + head0 + f / QD;
+          lse[k][r] = __ldcg(p.part_lse + row);
+          v[k][r] = __ldcg(reinterpret_cast<const float4*>(p.part_o + row * D) + f % QD);
+        } else {
+          lse[k][r] = NEG_INF;
+          v[k][r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kPerBatch; ++k) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (lse[k][r] == NEG_INF) continue;  // past c1 or past the group's columns
+        const float nm = fmaxf(m[r], lse[k][r]);
+        const float scale = exp2f(m[r] - nm);
+        const float w = exp2f(lse[k][r] - nm);
+        sum[r] = sum[r] * scale + w;
+        acc[r].x = acc[r].x * scale + w * v[k][r].x;
+        acc[r].y = acc[r].y * scale + w * v[k][r].y;
+        acc[r].z = acc[r].z * scale + w * v[k][r].z;
+        acc[r].w = acc[r].w * scale + w * v[k][r].w;
+        m[r] = nm;
+      }
+    }
+  }
+  __nv_bfloat16* ob = p.out + seq * p.o_st;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int f = lane + 32 * r;
+    if (f >= cols) continue;
+    const float inv = 1.f / sum[r];
+    __nv_bfloat16* dst = ob + static_cast<int64_t>(head0 + f / QD) * p.o_sh + (f % QD) * 4;
+    *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(acc[r].x * inv, acc[r].y * inv);
+    *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(acc[r].z * inv, acc[r].w * inv);
+  }
+}
+
 constexpr int kSmemPrefix = 1024;  // tile_indptr entries staged in shared memory (batch + 1 <= this)
 constexpr int kSmemPages = 1024;   // page ids of one CTA's tile range staged in shared memory
 
@@ -166,16 +259,27 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   int32_t* s_prefix = reinterpret_cast<int32_t*>(empty + STAGES);
   int32_t* s_pages = s_prefix + kSmemPrefix;
 
-  // launched with programmatic serialization: the plan and q come from earlier kernels; the merge
+  // launched with programmatic serialization: the plan and q come from earlier kernels; the next
   // kernel may be scheduled as soon as every CTA here has started
   grid_dependency_wait();
   grid_dependents_launch();
   const int c = blockIdx.x;
   const int kv0 = blockIdx.y * HPC;
   const int64_t total = p.header[0];
-  const int64_t t_begin = range_start(total, c, p.n_ctas);
-  const int64_t t_end = range_start(total, c + 1, p.n_ctas);
-  if (t_begin >= t_end) return;  // uniform over the block
+  // rows with no pages get a defined output of zeros (this CTA's heads of rows c, c + n_ctas, ...)
+  for (int b = c; b < p.batch; b += p.n_ctas) {
+    if (p.tile_indptr[b + 1] == p.tile_indptr[b]) {
+      const int h0 = kv0 * p.group;
+      for (int i = threadIdx.x; i < HPC * p.group * D; i += blockDim.x)
+        p.out[b * p.o_st + static_cast<int64_t>(h0 + i / D) * p.o_sh + i % D] = __float2bfloat16_rn(0.f);
+    }
+  }
+  // fewer tiles than CTAs: one tile each and the rest idle, so every range is non-empty and the
+  // CTAs covering a sequence are exactly c0..c1 of its first and last tiles
+  const int n = total < p.n_ctas ? static_cast<int>(total) : p.n_ctas;
+  if (c >= n) return;  // uniform over the block
+  const int64_t t_begin = range_start(total, c, n);
+  const int64_t t_end = range_start(total, c + 1, n);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -261,6 +365,7 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   int seq_t0 = prefix[seq];
   int seq_t1 = prefix[seq + 1];
   bool seg_open = false;
+  int fix_a = -1, fix_b = -1;  // split sequences whose ticket this warp completed
 
   // ldmatrix lane roles
   const int lm_j = lane >> 3;
@@ -437,137 +542,44 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
           if (2 * t4 < group) pl[ha] = m0 + log2f(lt0);
           if (2 * t4 + 1 < group) pl[ha + 1] = m1 + log2f(lt1);
         }
+        // count this warp in on the (sequence, KV head) ticket: the warp completing it has seen every
+        // covering CTA's partial (release by each arriving lane 0 after its warp's stores, acquire by
+        // the completing one) and combines them once its own tiles are done
+        __syncwarp();
+        const int c0 = owner_cta(total, n, seq_t0);
+        const int c1 = owner_cta(total, n, seq_t1 - 1);
+        int32_t* ticket = p.tickets + static_cast<int64_t>(seq) * p.hq + kvh;
+        int arrived = 0;
+        if (lane == 0) arrived = atomic_add_acq_rel_gpu(ticket, 1);
+        arrived = __shfl_sync(kFull, arrived, 0);
+        if (arrived == c1 - c0) {
+          if (lane == 0) *ticket = 0;  // ready for the next launch on this plan
+          // only a range's first and last segments can be split: at most two fix-ups per warp
+          if (fix_a < 0) fix_a = seq; else fix_b = seq;
+        }
       }
       seg_open = false;
     }
   }
-}
 
-// ------------------------------------------------------------------ merge
-// One CTA per sequence; sequences that one CTA covered whole exit at once.
-// The contributing CTAs (slot 2c when the sequence starts inside CTA c's
-// range, 2c + 1 otherwise) are visited in batches of kMergeBatch whose slots
-// and per-head lse are staged in shared memory: pass 1 finds each head's max
-// lse and weight sum, pass 2 accumulates out = sum_i w_i O_i / sum_i w_i,
-// w_i = 2^(lse_i - max lse), thread (head, 4 dims) issuing the loads of a
-// batch before using them.
-constexpr int kMergeBatch = 64;
-constexpr int kMergeHeads = 64;
-
-template <int D>
-__global__ void __launch_bounds__(256) decode_merge_kernel(DecodeArgs p) {
-  __shared__ int s_slot[kMergeBatch];
-  __shared__ float s_w[kMergeBatch * kMergeHeads];  // lse, then the weight, per (contributor, head)
-  __shared__ float s_max[kMergeHeads], s_inv[kMergeHeads];
-  grid_dependency_wait();  // the decode kernel's partials
-  const int seq = blockIdx.x;
-  const int64_t total = p.header[0];
-  const int n = p.n_ctas;
-  const int64_t tb0 = p.tile_indptr[seq];
-  const int64_t tb1 = p.tile_indptr[seq + 1];
-  if (tb1 <= tb0) {  // a row with no pages: defined output of zeros
-    for (int i = threadIdx.x; i < p.hq * D; i += blockDim.x)
-      p.out[seq * p.o_st + static_cast<int64_t>(i / D) * p.o_sh + i % D] = __float2bfloat16_rn(0.f);
-    return;
-  }
-  // CTA owning tile t: max c with floor(total*c/n) <= t
-  const int c0 = static_cast<int>(((tb0 + 1) * n + total - 1) / total) - 1;
-  const int c1 = static_cast<int>((tb1 * n + total - 1) / total) - 1;
-  if (c0 == c1) return;  // written directly by the decode kernel
-  const float NEG_INF = -__int_as_float(0x7f800000);
-  const int hq = p.hq;
-
-  // stage the slots and lse of contributors [cb, cb + nb)
-  auto stage = [&](int cb, int nb) {
-    __syncthreads();
-    if (threadIdx.x < nb) {
-      const int cc = cb + threadIdx.x;
-      const int64_t st = range_start(total, cc, n);
-      s_slot[threadIdx.x] = st != range_start(total, cc + 1, n) ? ((st >= tb0) ? 2 * cc : 2 * cc + 1) : -1;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < nb * hq; i += blockDim.x) {
-      const int k = i / hq, h = i % hq;
-      s_w[k * kMergeHeads + h] =
-          s_slot[k] >= 0 ? p.part_lse[static_cast<int64_t>(s_slot[k]) * hq + h] : NEG_INF;
-    }
-    __syncthreads();
-  };
-
-  // pass 1: per head, the max lse and the weight sum relative to it
-  float mx_h = NEG_INF, sum_h = 0.f;
-  for (int cb = c0; cb <= c1; cb += kMergeBatch) {
-    const int nb = min(kMergeBatch, c1 - cb + 1);
-    stage(cb, nb);
-    if (threadIdx.x < hq) {
-      const int h = threadIdx.x;
-      float bm = NEG_INF;
-      for (int k = 0; k < nb; ++k) bm = fmaxf(bm, s_w[k * kMergeHeads + h]);
-      const float nm = fmaxf(mx_h, bm);
-      sum_h *= mx_h == NEG_INF ? 0.f : exp2f(mx_h - nm);
-      mx_h = nm;
-      for (int k = 0; k < nb; ++k) sum_h += s_slot[k] >= 0 ? exp2f(s_w[k * kMergeHeads + h] - nm) : 0.f;
-    }
-  }
-  if (threadIdx.x < hq) {
-    s_max[threadIdx.x] = mx_h;
-    s_inv[threadIdx.x] = 1.f / sum_h;
-  }
-
-  // pass 2: the weighted sum of the partial outputs
-  const int per_thread = (hq * (D / 4) + blockDim.x - 1) / blockDim.x;  // (head, 4 dims) items per thread
-  float4 acc[4];
-#pragma unroll
-  for (int r = 0; r < 4; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int cb = c0; cb <= c1; cb += kMergeBatch) {
-    const int nb = min(kMergeBatch, c1 - cb + 1);
-    if (c1 - c0 + 1 > kMergeBatch) {
-      stage(cb, nb);
-    } else {
-      __syncthreads();  // one batch: pass 1 left its slots and lse staged; s_max is written
-    }
-    for (int i = threadIdx.x; i < nb * hq; i += blockDim.x) {
-      const int k = i / hq, h = i % hq;
-      s_w[k * kMergeHeads + h] = s_slot[k] >= 0 ? exp2f(s_w[k * kMergeHeads + h] - s_max[h]) : 0.f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int idx = threadIdx.x + r * blockDim.x;
-      if (r >= per_thread || idx >= hq * (D / 4)) continue;
-      const int h = idx / (D / 4);
-      const int d = (idx % (D / 4)) * 4;
-      for (int k0 = 0; k0 < nb; k0 += 8) {
-        float4 v[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int sl = k0 + k < nb ? s_slot[k0 + k] : -1;
-          v[k] = sl >= 0 ? *reinterpret_cast<const float4*>(p.part_o + (static_cast<int64_t>(sl) * hq + h) * D + d)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          if (k0 + k < nb) {
-            const float w = s_w[(k0 + k) * kMergeHeads + h];
-            acc[r].x += w * v[k].x;
-            acc[r].y += w * v[k].y;
-            acc[r].z += w * v[k].z;
-            acc[r].w += w * v[k].w;
-          }
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int idx = threadIdx.x + r * blockDim.x;
-    if (r >= per_thread || idx >= hq * (D / 4)) continue;
-    const int h = idx / (D / 4);
-    const int d = (idx % (D / 4)) * 4;
-    const float inv = s_inv[h];
-    __nv_bfloat16* ob = p.out + seq * p.o_st + static_cast<int64_t>(h) * p.o_sh + d;
-    *reinterpret_cast<__nv_bfloat162*>(ob) = __floats2bfloat162_rn(acc[r].x * inv, acc[r].y * inv);
-    *reinterpret_cast<__nv_bfloat162*>(ob + 2) = __floats2bfloat162_rn(acc[r].z * inv, acc[r].w * inv);
+  // deferred fix-ups: the accumulators are dead here, so the combine does not raise the register
+  // footprint of the tile loop
+  __syncwarp();
+  for (int f = 0; f < 2; ++f) {
+    const int fs = f == 0 ? fix_a : fix_b;
+    if (fs < 0) continue;
+    const int f_t0 = prefix[fs], f_t1 = prefix[fs + 1];
+    const int c0 = owner_cta(total, n, f_t0);
+    const int c1 = owner_cta(total, n, f_t1 - 1);
+    const int cols = group * (D / 4);
+    if (cols <= 32)
+      fixup_sequence<D, 1>(p, fs, kvh, total, n, c0, c1, f_t0, lane);
+    else if (cols <= 64)
+      fixup_sequence<D, 2>(p, fs, kvh, total, n, c0, c1, f_t0, lane);
+    else if (cols <= 128)
+      fixup_sequence<D, 4>(p, fs, kvh, total, n, c0, c1, f_t0, lane);
+    else
+      fixup_sequence<D, 8>(p, fs, kvh, total, n, c0, c1, f_t0, lane);
   }
 }
 
@@ -621,11 +633,6 @@ int launch_decode(const CUtensorMap& map, DecodeArgs a, int groups, int max_ctas
     set_last_error("decode_attention", err);
     return NQT_ERR_CUDA;
   }
-  err = launch_pdl(decode_merge_kernel<D>, dim3(a.batch), dim3(256), 0, s, a);
-  if (err != cudaSuccess) {
-    set_last_error("decode_merge", err);
-    return NQT_ERR_CUDA;
-  }
   return NQT_OK;
 }
 
@@ -664,9 +671,10 @@ extern "C" int nqt_decode_plan(const int32_t* kv_indptr, const int32_t* last_pag
   const WsLayout w = ws_layout(batch_capacity, num_qo_heads, head_dim);
   if (workspace_bytes < w.total) return NQT_ERR_CAPACITY;
   uint8_t* base = static_cast<uint8_t*>(workspace);
-  decode_plan_kernel<<<1, 1024, 0, as_stream(stream)>>>(kv_indptr, last_page_len, batch, page_size,
-                                                         reinterpret_cast<int32_t*>(base),
-                                                         reinterpret_cast<int32_t*>(base + w.tile_indptr));
+  decode_plan_kernel<<<1, 1024, 0, as_stream(stream)>>>(
+      kv_indptr, last_page_len, batch, page_size, reinterpret_cast<int32_t*>(base),
+      reinterpret_cast<int32_t*>(base + w.tile_indptr), reinterpret_cast<int32_t*>(base + w.tickets),
+      batch * num_qo_heads);
   return check_launch("decode_plan");
 }
 
@@ -682,8 +690,6 @@ int check_decode_args(const void* q, int64_t q_stride_tok, int64_t q_stride_head
   if (num_kv_heads < 1 || num_qo_heads % num_kv_heads) return NQT_ERR_ARG;
   if (num_qo_heads / num_kv_heads > 8 || num_kv_heads > 256) return NQT_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return NQT_ERR_UNSUPPORTED;
-  // the merge kernel stages per-head weights of kMergeHeads heads and holds <= 4 items per thread
-  if (num_qo_heads > kMergeHeads || num_qo_heads * head_dim / 4 > 4 * 256) return NQT_ERR_UNSUPPORTED;
   if (page_size < kTok || page_size % kTok || page_size > 256) return NQT_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(layer_cache) & 15) || (reinterpret_cast<uintptr_t>(q) & 3)) return NQT_ERR_ARG;
   if ((q_stride_tok & 1) || (q_stride_head & 1)) return NQT_ERR_ARG;
@@ -713,6 +719,7 @@ int run_decode(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const
   a.last_len = last_page_len;
   a.tile_indptr = reinterpret_cast<const int32_t*>(base + w.tile_indptr);
   a.header = reinterpret_cast<const int32_t*>(base);
+  a.tickets = reinterpret_cast<int32_t*>(base + w.tickets);
   a.part_lse = reinterpret_cast<float*>(base + w.part_lse);
   a.part_o = reinterpret_cast<float*>(base + w.part_o);
   a.status = status;
@@ -775,9 +782,10 @@ constexpr int kNoAllocMaxBatch = 1024;     // rows per call
 constexpr int kNoAllocMaxHeads = 32;       // num_qo_heads
 constexpr int kNoAllocMaxHeadsDim = 2048;  // num_qo_heads * head_dim
 constexpr int kNoAllocMaxCtas = 296;       // split CTAs per KV-head group (2 per SM on 148 SMs)
+// the layout grows with num_qo_heads at a fixed num_qo_heads * head_dim, so the widest head count bounds
+// every allowed shape (header, tile prefix, tickets, lse, partial O: about 5.1 MB)
 constexpr size_t kNoAllocScratchBytes =
-    kHeaderBytes + 4352 + 256 + 4ull * 2 * kNoAllocMaxCtas * kNoAllocMaxHeads + 256 +
-    4ull * 2 * kNoAllocMaxCtas * kNoAllocMaxHeadsDim;  // header + tile prefix + lse + partial O (about 4.8 MB)
+    ws_layout(kNoAllocMaxBatch, kNoAllocMaxHeads, kNoAllocMaxHeadsDim / kNoAllocMaxHeads, kNoAllocMaxCtas).total;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -835,7 +843,8 @@ extern "C" int nqt_decode_attention_noalloc(const void* q, int64_t q_stride_tok,
   if (rc != NQT_OK) return rc;
   cudaStream_t s = as_stream(stream);
   decode_plan_kernel<<<1, 1024, 0, s>>>(kv_indptr, last_page_len, batch, page_size, reinterpret_cast<int32_t*>(base),
-                                        reinterpret_cast<int32_t*>(base + w.tile_indptr));
+                                        reinterpret_cast<int32_t*>(base + w.tile_indptr),
+                                        reinterpret_cast<int32_t*>(base + w.tickets), batch * num_qo_heads);
   rc = check_launch("nqt_decode_attention_noalloc: plan");
   if (rc != NQT_OK) return rc;
   return run_decode(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr, kv_indices,
