@@ -47,6 +47,9 @@ extern "C" {
 #define NQT_DEV_TABLE_FULL 0x10   /* planner: a request outgrew its page-table row */
 #define NQT_DEV_CAPACITY 0x20     /* metadata outgrew a static buffer */
 
+/* nqt_decode_attention_ex flags */
+#define NQT_DECODE_OVERLAP_KV_WRITE 0x1 /* see nqt_decode_attention_ex */
+
 /* element types */
 #define NQT_BF16 0
 #define NQT_F16 1
@@ -119,7 +122,8 @@ int nqt_decode_plan(
 
 /*
  * Paged GQA decode attention (one query per row), split-KV with TMA page
- * gathers into shared memory and an LSE merge.  Replaces
+ * gathers into shared memory; split rows are combined by LSE inside the
+ * same launch (the last covering CTA finishes them).  Replaces
  * BatchDecodeWithPagedKVCacheWrapper.run (executor/talker_kv.py:305-306).
  * q/out: [batch, num_qo_heads, head_dim] bf16 with token/head strides.
  * layer_cache: contiguous [total_pages, 2, page_size, num_kv_heads, head_dim]
@@ -136,6 +140,31 @@ int nqt_decode_attention(
     float sm_scale,
     void* out, int64_t out_stride_tok, int64_t out_stride_head,
     void* workspace, size_t workspace_bytes,
+    int32_t* status, void* stream);
+
+/*
+ * nqt_decode_attention with launch flags; flags = 0 is nqt_decode_attention.
+ * Same reference interface (BatchDecodeWithPagedKVCacheWrapper.run,
+ * executor/talker_kv.py:305-306), called right after the layer's K/V write
+ * (attend, executor/talker_kv.py:104-130, writes K/V at :116, then runs
+ * the wrapper).
+ * NQT_DECODE_OVERLAP_KV_WRITE: the kernel may start while the kernel before
+ * it on the stream is still running, and reads the plan in the workspace,
+ * kv_indptr, kv_indices, last_page_len and every KV tile except each row's
+ * last 16-token tile before that kernel has finished; q, each row's last
+ * tile and all of its writes wait for it.  Pass it only when the previous
+ * kernel writes none of the former, e.g. when it is
+ * nqt_qk_norm_rope_paged_kv_write of one decode token per row (that token
+ * lies in its row's last tile), or another decode launch on the same plan.
+ */
+int nqt_decode_attention_ex(
+    const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+    const void* layer_cache, int total_pages, int page_size,
+    const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* last_page_len,
+    int batch, int batch_capacity, int num_qo_heads, int num_kv_heads, int head_dim,
+    float sm_scale,
+    void* out, int64_t out_stride_tok, int64_t out_stride_head,
+    void* workspace, size_t workspace_bytes, int flags,
     int32_t* status, void* stream);
 
 /*

@@ -56,6 +56,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         I,
         [P, L, L, P, I, I, P, P, P, I, I, I, I, I, F, P, L, L, P, Z, P, P],
     ),
+    "nqt_decode_attention_ex": (
+        I,
+        [P, L, L, P, I, I, P, P, P, I, I, I, I, I, F, P, L, L, P, Z, I, P, P],
+    ),
     "nqt_decode_attention_noalloc": (
         I,
         [P, L, L, P, I, I, P, P, P, I, I, I, I, F, P, L, L, P, P],
@@ -142,8 +146,7 @@ def exported_symbols() -> list[str]:
 
 # kernels each entry point launches (nqt_plan_step adds the split-KV plan when given a workspace)
 KERNELS_PER_CALL = {
-    "nqt_decode_attention": 2,
-    "nqt_decode_attention_noalloc": 3,
+    "nqt_decode_attention_noalloc": 2,
 }
 _launches = 0
 

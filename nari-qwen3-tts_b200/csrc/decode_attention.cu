@@ -77,6 +77,7 @@ struct DecodeArgs {
   float* part_o;
   int32_t* status;
   int batch, hq, hkv, group, page_size, total_pages, n_ctas;
+  int early;  // NQT_DECODE_OVERLAP_KV_WRITE: read the plan and older tiles before the dependency wait
   float scale_log2;
 };
 
@@ -259,9 +260,12 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   int32_t* s_prefix = reinterpret_cast<int32_t*>(empty + STAGES);
   int32_t* s_pages = s_prefix + kSmemPrefix;
 
-  // launched with programmatic serialization: the plan and q come from earlier kernels; the next
-  // kernel may be scheduled as soon as every CTA here has started
-  grid_dependency_wait();
+  // Launched with programmatic serialization; the next kernel may be scheduled as soon as every CTA
+  // here has started.  By default everything waits for the previous grid.  With `early` the caller
+  // guarantees that the previous grid writes neither the plan, the page table nor any KV tile but each
+  // row's last: those are read before the wait (page-id staging and the first TMA loads overlap the
+  // previous kernel), while q, each row's last tile and every write here come after it.
+  if (!p.early) grid_dependency_wait();
   grid_dependents_launch();
   const int c = blockIdx.x;
   const int kv0 = blockIdx.y * HPC;
@@ -269,6 +273,7 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   // rows with no pages get a defined output of zeros (this CTA's heads of rows c, c + n_ctas, ...)
   for (int b = c; b < p.batch; b += p.n_ctas) {
     if (p.tile_indptr[b + 1] == p.tile_indptr[b]) {
+      if (p.early) grid_dependency_wait();
       const int h0 = kv0 * p.group;
       for (int i = threadIdx.x; i < HPC * p.group * D; i += blockDim.x)
         p.out[b * p.o_st + static_cast<int64_t>(h0 + i / D) * p.o_sh + i % D] = __float2bfloat16_rn(0.f);
@@ -320,6 +325,7 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
     int seq_t0 = prefix[seq];
     int seq_t1 = prefix[seq + 1];
     int seq_base = p.indptr[seq];
+    bool dependency_met = !p.early;
     for (int i = 0; i < n_tiles; ++i) {
       const int64_t t = t_begin + i;
       while (t >= seq_t1) {  // advance to the owning sequence (skips empty rows)
@@ -327,6 +333,10 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
         seq_t0 = seq_t1;
         seq_t1 = prefix[seq + 1];
         seq_base = p.indptr[seq];
+      }
+      if (!dependency_met && t == seq_t1 - 1) {  // a row's last tile may come from the previous grid
+        grid_dependency_wait();
+        dependency_met = true;
       }
       const int s = i % STAGES;
       // warp-uniform decision: every lane reaches the same __syncwarp
@@ -371,6 +381,7 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   const int lm_j = lane >> 3;
   const int lm_r = lane & 7;
 
+  if (p.early) grid_dependency_wait();  // q, and the partials and tickets of the previous launch
   for (int i = 0; i < n_tiles; ++i) {
     const int64_t t = t_begin + i;
     while (t >= seq_t1) {
@@ -703,7 +714,7 @@ int run_decode(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const
                int total_pages, int page_size, const int32_t* kv_indptr, const int32_t* kv_indices,
                const int32_t* last_page_len, int batch, int num_qo_heads, int num_kv_heads, int head_dim,
                float sm_scale, void* out, int64_t out_stride_tok, int64_t out_stride_head, uint8_t* base,
-               const WsLayout& w, int max_ctas, int32_t* status, cudaStream_t s) {
+               const WsLayout& w, int max_ctas, int early, int32_t* status, cudaStream_t s) {
   CUtensorMap map;
   int rc = encode_layer_map(&map, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
   if (rc != NQT_OK) return rc;
@@ -730,11 +741,33 @@ int run_decode(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const
   a.page_size = page_size;
   a.total_pages = total_pages;
   a.n_ctas = 1;
+  a.early = early;
   a.scale_log2 = sm_scale * 1.4426950408889634f;
   return head_dim == 128 ? dispatch_hpc<128>(map, a, max_ctas, s) : dispatch_hpc<64>(map, a, max_ctas, s);
 }
 
 }  // namespace
+
+extern "C" int nqt_decode_attention_ex(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                                       const void* layer_cache, int total_pages, int page_size,
+                                       const int32_t* kv_indptr, const int32_t* kv_indices,
+                                       const int32_t* last_page_len, int batch, int batch_capacity,
+                                       int num_qo_heads, int num_kv_heads, int head_dim, float sm_scale, void* out,
+                                       int64_t out_stride_tok, int64_t out_stride_head, void* workspace,
+                                       size_t workspace_bytes, int flags, int32_t* status, void* stream) {
+  int rc = check_decode_args(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr,
+                             kv_indices, last_page_len, out, out_stride_tok, out_stride_head, batch, num_qo_heads,
+                             num_kv_heads, head_dim);
+  if (rc != NQT_OK) return rc;
+  if (!workspace || batch > batch_capacity) return NQT_ERR_ARG;
+  if (flags & ~NQT_DECODE_OVERLAP_KV_WRITE) return NQT_ERR_ARG;
+  const WsLayout w = ws_layout(batch_capacity, num_qo_heads, head_dim);
+  if (workspace_bytes < w.total) return NQT_ERR_CAPACITY;
+  return run_decode(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr, kv_indices,
+                    last_page_len, batch, num_qo_heads, num_kv_heads, head_dim, sm_scale, out, out_stride_tok,
+                    out_stride_head, static_cast<uint8_t*>(workspace), w, kMaxSplitCtas,
+                    (flags & NQT_DECODE_OVERLAP_KV_WRITE) ? 1 : 0, status, as_stream(stream));
+}
 
 extern "C" int nqt_decode_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                                     const void* layer_cache, int total_pages, int page_size,
@@ -743,17 +776,10 @@ extern "C" int nqt_decode_attention(const void* q, int64_t q_stride_tok, int64_t
                                     int num_kv_heads, int head_dim, float sm_scale, void* out,
                                     int64_t out_stride_tok, int64_t out_stride_head, void* workspace,
                                     size_t workspace_bytes, int32_t* status, void* stream) {
-  int rc = check_decode_args(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr,
-                             kv_indices, last_page_len, out, out_stride_tok, out_stride_head, batch, num_qo_heads,
-                             num_kv_heads, head_dim);
-  if (rc != NQT_OK) return rc;
-  if (!workspace || batch > batch_capacity) return NQT_ERR_ARG;
-  const WsLayout w = ws_layout(batch_capacity, num_qo_heads, head_dim);
-  if (workspace_bytes < w.total) return NQT_ERR_CAPACITY;
-  return run_decode(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr, kv_indices,
-                    last_page_len, batch, num_qo_heads, num_kv_heads, head_dim, sm_scale, out, out_stride_tok,
-                    out_stride_head, static_cast<uint8_t*>(workspace), w, kMaxSplitCtas, status,
-                    as_stream(stream));
+  return nqt_decode_attention_ex(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr,
+                                 kv_indices, last_page_len, batch, batch_capacity, num_qo_heads, num_kv_heads,
+                                 head_dim, sm_scale, out, out_stride_tok, out_stride_head, workspace,
+                                 workspace_bytes, 0, status, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -849,5 +875,5 @@ extern "C" int nqt_decode_attention_noalloc(const void* q, int64_t q_stride_tok,
   if (rc != NQT_OK) return rc;
   return run_decode(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr, kv_indices,
                     last_page_len, batch, num_qo_heads, num_kv_heads, head_dim, sm_scale, out, out_stride_tok,
-                    out_stride_head, base, w, kNoAllocMaxCtas, status, s);
+                    out_stride_head, base, w, kNoAllocMaxCtas, 0, status, s);
 }

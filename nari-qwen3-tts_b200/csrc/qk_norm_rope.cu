@@ -71,6 +71,9 @@ template <typename T, int D>
 __global__ void __launch_bounds__(256) qk_norm_rope_paged_kernel(const __grid_constant__ QkArgs a, T* cache, int total_pages,
                                                                  int page_size, const int64_t* write_pages,
                                                                  const int64_t* write_offsets) {
+  // a decode launch queued behind this one with NQT_DECODE_OVERLAP_KV_WRITE may start its page-id
+  // staging and older-tile loads now; it waits for this grid before touching q or a row's last tile
+  grid_dependents_launch();
   const int token = blockIdx.x;
   const int ph = blockIdx.y * 8 + (threadIdx.x >> 5);
   if (ph >= a.hq + a.hkv) return;

@@ -30,6 +30,9 @@ from . import _lib
 from ._lib import call, ptr
 from .kernels import device_status, paired_qk_norm_rope_paged_cache_
 
+# nqt_decode_attention_ex flag (include/nqt.h NQT_DECODE_OVERLAP_KV_WRITE)
+DECODE_OVERLAP_KV_WRITE = 0x1
+
 
 @dataclass(frozen=True, slots=True)
 class TalkerAttentionMetadata:
@@ -70,9 +73,16 @@ def batch_decode_paged(
     sm_scale: float | None = None,
     out: torch.Tensor | None = None,
     plan: bool = True,
+    overlap_kv_write: bool = False,
 ) -> torch.Tensor:
     """Paged GQA decode attention, one query per row (FlashInfer decode
-    wrapper semantics: all (n_pages - 1) * P + last_page_len tokens)."""
+    wrapper semantics: all (n_pages - 1) * P + last_page_len tokens).
+
+    ``overlap_kv_write``: the kernel issued just before on this stream writes
+    no KV tile but each row's last, and neither the page table nor the plan
+    (the one-token-per-row K/V write of a decode step, or another decode
+    launch on the same plan); the decode kernel then stages page ids and
+    streams the older tiles while that kernel finishes."""
 
     rows, hq, d = query.shape
     pages, kinds, page_size, hkv, d2 = layer_cache.shape
@@ -94,7 +104,7 @@ def batch_decode_paged(
             ptr(workspace), workspace.numel() * workspace.element_size(), stream,
         )
     call(
-        "nqt_decode_attention",
+        "nqt_decode_attention_ex",
         ptr(query), query.stride(0), query.stride(1),
         ptr(layer_cache), pages, page_size,
         ptr(kv_indptr), ptr(kv_indices), ptr(last_page_len),
@@ -102,6 +112,8 @@ def batch_decode_paged(
         float(sm_scale if sm_scale is not None else d**-0.5),
         ptr(out), out.stride(0), out.stride(1),
         ptr(workspace), workspace.numel() * workspace.element_size(),
+        # a plan made just above is the previous kernel: it must be complete before anything is read
+        DECODE_OVERLAP_KV_WRITE if overlap_kv_write and not plan else 0,
         ptr(device_status(device)), stream,
     )
     return out
@@ -296,6 +308,7 @@ class B200TalkerBinding:
                 self.paged_kv_last_page_len,
                 batch=self.capture_batch_size,
             )
+        # attend() has just written each row's one new token (its last tile) with the K/V write kernel
         return batch_decode_paged(
             query.to(self.dtype),
             layer,
@@ -305,6 +318,7 @@ class B200TalkerBinding:
             self.decode_workspace,
             batch_capacity=self.capture_batch_size,
             plan=False,
+            overlap_kv_write=True,
         )
 
     @staticmethod

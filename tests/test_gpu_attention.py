@@ -221,3 +221,37 @@ def test_short_cache_golden_fixture(nqt, cuda, golden):
     out = nqt.decode_attn_nhd_short_cache(g["q"].to(torch.bfloat16).to(cuda), g["k_cache"].to(torch.bfloat16).to(cuda),
                                           g["v_cache"].to(torch.bfloat16).to(cuda), g["length"])
     torch.testing.assert_close(out.float().cpu(), g["out"], atol=ATOL, rtol=0)
+
+
+def test_decode_overlapping_the_kv_write_sees_each_new_token(nqt, cuda):
+    """The decode step's order (attend, executor/talker_kv.py:104-130): the K/V write of each row's one new
+    token, then the decode launch.  With overlap_kv_write the decode stages page ids and streams the older
+    tiles while the write kernel still runs; the new token (in each row's last tile) and q must still be
+    the written ones, so the result equals the oracle on the updated cache and, bit for bit, the launch
+    that waits for the write kernel first."""
+    hq, hkv, d, P = 16, 8, 128, 16
+    g = torch.Generator().manual_seed(21)
+    lens = torch.randint(1, 1500, (48,), generator=g).tolist() + [1, 16, 17, 32, 33, 2047, 2048, 2049]
+    rows = len(lens)
+    cache, indptr, indices, last = make_paged(lens, page_size=P, hkv=hkv, d=d, seed=21)
+    pos = torch.tensor(lens) - 1
+    wp = indices[indptr[:-1].long() + pos // P].long()
+    wo = pos % P
+    cache_dev = cache.to(cuda)
+    meta = [x.to(cuda) for x in (indptr, indices, last)]
+    ws = torch.zeros(nqt.lib().nqt_decode_workspace_bytes(rows, hq, d), dtype=torch.uint8, device=cuda)
+    out_a = torch.empty(rows, hq, d, dtype=torch.bfloat16, device=cuda)
+    out_b = torch.empty_like(out_a)
+    for step in range(4):
+        qkv, qw, kw = _qk_inputs(rows, hq, hkv, d, 100 + step)
+        qkv = qkv.to(cuda)
+        q, k, v = _split(qkv, hq, hkv, d)
+        nqt.paired_qk_norm_rope_paged_cache_(q, k, v, qw.to(cuda), kw.to(cuda), pos.to(cuda), 1e-6, 1e6,
+                                             cache_dev, wp.to(cuda), wo.to(cuda))
+        nqt.batch_decode_paged(q, cache_dev, *meta, ws, out=out_a, plan=step == 0, overlap_kv_write=True)
+        nqt.batch_decode_paged(q, cache_dev, *meta, ws, out=out_b, plan=False)
+        torch.cuda.synchronize()
+        assert torch.equal(out_a, out_b), step
+        want = oatt.paged_decode(q.float().cpu(), cache_dev.float().cpu(), indptr, indices, last)
+        torch.testing.assert_close(out_a.float().cpu(), want, atol=ATOL, rtol=0)
+    assert nqt.kernels.read_status(cuda) == 0
