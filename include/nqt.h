@@ -408,16 +408,19 @@ int nqt_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, int
  *   epilogue 2  (weight packed with interleave_gate_up) Y[m, f] =
  *               silu(g) * up, g and up rounded to bf16 (the gate_up GEMM
  *               followed by nqt_silu_and_mul); Y is [m, n / 2].
- * n % 128 == 0, k % 64 == 0, n * round_up(m, 4) <= 4 Mi; x and the packed weight 16-byte
- * aligned, ldx (elements) a multiple of 8.  ctas = size of the persistent
- * stream-K grid (<= 0: one per SM).  Tiles shared by several CTAs are summed
- * in a per-device static workspace, so the calls of one device are ordered
- * on one stream.  Launched with programmatic stream serialization.
+ * 1 <= m <= 256, n % 128 == 0, k % 64 == 0; x and the packed weight
+ * 16-byte aligned, ldx (elements) a multiple of 8.  split = CTAs (one
+ * thread-block cluster) that share each 128-row tile's K and sum their fp32
+ * partials through distributed shared memory, 1..8; 0 picks the largest
+ * power of two that keeps the grid within one CTA per SM.  No workspace:
+ * calls on different streams may overlap.  Launched with programmatic
+ * stream serialization (the weight copies start before the previous kernel
+ * has finished).
  */
 int nqt_gemm_pack_weight(const void* w, int64_t ldw, int n, int k, int interleave_gate_up, void* packed,
                          void* stream);
 int nqt_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, void* y, int64_t ldy, const void* bias,
-                  int m, int n, int k, int epilogue, int ctas, int32_t* status, void* stream);
+                  int m, int n, int k, int epilogue, int split, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

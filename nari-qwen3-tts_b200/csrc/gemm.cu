@@ -10,33 +10,34 @@
 //
 // W is packed once, at load time, into 16 KB units [N / 128][K / 64][128 rows
 // x 128 B] stored contiguously and already in the 128-byte-swizzled order the
-// MMA reads (16-byte chunk c of row r at chunk c ^ (r % 8)).  The units of all
-// tiles form one array, and a persistent grid of one CTA per SM splits it into
-// equal contiguous ranges (stream-K): every SM streams the same number of
-// bytes with one bulk copy per stage, whatever N / 128 is.  A CTA's range
-// covers pieces of one to a few tiles; a tile covered by one CTA is written
-// directly, a tile shared by several is summed with fp32 reductions into a
-// zeroed L2-resident workspace (16-byte reductions, token-contiguous rows),
-// and the CTA that arrives last (a per-tile ticket) writes the output and
-// zeroes its part of the workspace again.  X
-// (the step's activations, L2-resident) comes through a 2-D tensor map (box
-// 64 x Mpad, 128-byte swizzle).
+// MMA reads (16-byte chunk c of row r at chunk c ^ (r % 8)), so a stage is one
+// bulk copy.  X (the step's activations, L2-resident) comes through a 2-D
+// tensor map (box 64 x Mpad, 128-byte swizzle).
 //
-// Warp roles (6 warps): 0 copy producer, 1 TMEM owner + MMA issuer (two TMEM
-// accumulators, so the next tile piece accumulates while the epilogue drains
-// the previous one), 2-5 the epilogue (warp w reads TMEM lanes 32 (w % 4) ..).
-// Epilogues:
+// Work split.  The grid is (N / 128 tiles) x S, one thread-block cluster of S
+// CTAs per tile (S <= 8, chosen so the grid is about one CTA per SM): CTA r
+// of a cluster streams the r-th contiguous K slice of the tile, with every
+// stage of a short slice in flight at once.  The S fp32 partials are summed
+// through distributed shared memory: each CTA parks its partial D^T
+// token-major in its own shared memory, and after a cluster barrier CTA r
+// reduces tokens [r m / S, (r+1) m / S) over the S partials (16-byte remote
+// loads), applies the epilogue and writes Y.  No global workspace, atomics or
+// second pass.
+//
+// Warp roles (6 warps): 0 copy producer, 1 TMEM owner + MMA issuer, 2-5 the
+// epilogue (warp w reads TMEM lanes 32 (w % 4) ..).  Epilogues:
 //   plain    Y = bf16(acc)
 //   bias     Y = bf16(acc + bias)                       (nn.Linear with bias)
 //   silu_mul W rows interleaved in 64-row blocks [gate 64 | up 64]; output
 //            column f of block b is silu(g) * u of rows 128 b + f, 128 b + 64 + f,
 //            with g and u rounded to bf16 first (the unfused gate_up GEMM
 //            followed by silu_and_mul); Y is [M, N / 2].
-// Every wait is bounded and reports NQT_DEV_TIMEOUT.  The kernel is launched
-// with programmatic stream serialization: the W stages of the prologue are
-// fetched before griddepcontrol.wait, everything that touches X, Y or the
-// workspace after it.  The workspace is one per device, so calls on a device
-// are ordered on one stream.
+// Every mbarrier wait is bounded and reports NQT_DEV_TIMEOUT; on a timeout a
+// thread skips its remaining work but still reaches every cluster barrier, so
+// no CTA leaves while a peer may read its shared memory.  The kernel is
+// launched with programmatic stream serialization: the W copies are issued
+// before griddepcontrol.wait (the weights do not depend on the previous
+// kernel), X, Y and everything after them come after it.
 //
 // Replaces the torch/cuBLAS projections of the decoder layers
 // (model/layers.py:195-270, model/components.py:300-356) and the sm90-only
@@ -55,12 +56,10 @@ constexpr int kTileN = 128;                    // W rows per tile (MMA M)
 constexpr int kBlockK = 64;                    // K per unit (one 128-byte swizzle row)
 constexpr int kThreads = 6 * 32;
 constexpr int kWBytes = kTileN * kBlockK * 2;  // 16 KB per unit
-constexpr int kXsBytes = 32 * kTileN * 2;      // epilogue staging: 32 tokens x 128 bf16
-constexpr int kMaxWsFloats = 4 << 20;          // split-tile workspace, fp32 [N][round_up(M, 4)]
-constexpr int kMaxTiles = 1024;
-
-__device__ __align__(16) float g_ws[kMaxWsFloats];  // zero at load; each split tile's last CTA zeroes it again
-__device__ int g_ws_ticket[kMaxTiles];  // CTAs done per split tile; reset by the last one
+constexpr int kMaxSplit = 8;                   // portable cluster size
+constexpr int kSmemBudget = 227 * 1024;
+constexpr int kMaxGroup = 4;   // K units per stage: one W copy of up to 64 KB, one X copy
+constexpr int kMaxStages = 8;
 
 enum Epilogue : int { kPlain = 0, kBias = 1, kSiluMul = 2 };
 
@@ -70,28 +69,28 @@ struct GemmArgs {
   int64_t ldy;
   const __nv_bfloat16* bias;
   int32_t* status;
-  float* ws;
-  int* ticket;
   int m, n, k;
   int mpad;  // MMA N: m rounded up to 16
   int epilogue;
   int stages;
-  int kbt;      // K units per tile
-  int units;    // tiles * kbt
-  int vec_out;  // y rows 16-byte aligned: vector stores
-  int ldws;     // workspace row pitch: m rounded up to 4
+  int kbt;    // K units per tile
+  int own;    // tokens per cluster rank, own_tokens(m, S)
+  int group;  // K units per stage (one W bulk copy, one X tensor load)
 };
 
 __host__ __device__ constexpr int x_bytes(int mpad) { return mpad * kBlockK * 2; }
-__host__ __device__ constexpr int stage_bytes(int mpad) { return kWBytes + x_bytes(mpad); }
-
-// Units [first_unit(c), first_unit(c + 1)) belong to CTA c of G.
-__device__ __forceinline__ int first_unit(int c, int units, int G) {
-  return static_cast<int>((static_cast<int64_t>(c) * units) / G);
-}
-// The CTA whose range holds unit u.
-__device__ __forceinline__ int cta_of(int u, int units, int G) {
-  return static_cast<int>(((static_cast<int64_t>(u) + 1) * G - 1) / units);
+// a stage: `group` W units [group][128 x 128 B] then their X slabs [group][mpad x 128 B]
+__host__ __device__ constexpr int stage_bytes(int mpad, int group) { return group * (kWBytes + x_bytes(mpad)); }
+// Tokens each CTA of a cluster of S finishes, and the receive buffer that holds every sender's fp32
+// slice of them: [S senders][own tokens][128 rows].  The sender parks its whole partial the same way,
+// [S * own tokens][128 rows], over its drained stage ring.
+__host__ __device__ constexpr int own_tokens(int m, int S) { return (m + S - 1) / S; }
+__host__ __device__ constexpr int park_bytes(int m, int S) { return S * own_tokens(m, S) * kTileN * 4; }
+// a CTA alone (S = 1) sums nothing and reads its own parked partial
+__host__ __device__ constexpr int recv_bytes(int m, int S) { return S > 1 ? park_bytes(m, S) : 0; }
+__host__ __device__ constexpr int ring_bytes(int mpad, int group, int m, int S, int stages) {
+  return stages * stage_bytes(mpad, group) > park_bytes(m, S) ? stages * stage_bytes(mpad, group)
+                                                               : park_bytes(m, S);
 }
 
 // Contiguous global -> shared copy completing on an mbarrier (16-byte aligned, size % 16 == 0).
@@ -102,303 +101,236 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+// X slabs [c2, c2 + group) of the 3-D view {64 k, m rows, k / 64 slabs} (one copy per stage)
+__device__ __forceinline__ void tma_load_x(void* dst, const CUtensorMap* map, uint64_t* bar, int slab) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(0), "r"(0), "r"(slab)
       : "memory");
 }
 
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Cluster barrier, split: every thread of every CTA arrives, then waits (release / acquire at cluster scope).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+
+// Contiguous copy from this CTA's shared memory into a peer's, completing `bar_cluster_addr`'s
+// transaction count there (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster_addr, const void* src, uint32_t bytes,
+                                                  uint32_t bar_cluster_addr) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster_addr),
+               "r"(smem_addr(src)), "r"(bytes), "r"(bar_cluster_addr)
                : "memory");
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + __expf(-g)) * u; }
 
 __device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
-
-// Writes rows [0, 32) of the staging buffer (32 tokens x `cols` bf16, row pitch 128) to Y[m0 + r][col0 ..].
-__device__ __forceinline__ void store_staged(const GemmArgs& a, const __nv_bfloat16* xs, int m0, int col0, int cols,
-                                             int et) {
-  if (a.vec_out) {
-    const int per_row = cols / 8;
-    for (int i = et; i < 32 * per_row; i += 128) {
-      const int r = i / per_row, ch = i % per_row;
-      if (m0 + r < a.m) {
-        *reinterpret_cast<uint4*>(a.y + static_cast<int64_t>(m0 + r) * a.ldy + col0 + ch * 8) =
-            *reinterpret_cast<const uint4*>(xs + r * kTileN + ch * 8);
-      }
-    }
-  } else {
-    for (int i = et; i < 32 * cols; i += 128) {
-      const int r = i / cols, c = i % cols;
-      if (m0 + r < a.m) a.y[static_cast<int64_t>(m0 + r) * a.ldy + col0 + c] = xs[r * kTileN + c];
-    }
-  }
-}
-
-// A tile written by one CTA: TMEM -> bf16 (epilogue) -> staging -> Y.
-__device__ void direct_epilogue(const GemmArgs& a, uint32_t t_row, int row, int tile, __nv_bfloat16* xs, int et) {
-  const int n0 = tile * kTileN;
-  const float bias = a.epilogue == kBias ? __bfloat162float(a.bias[n0 + row]) : 0.f;
-  for (int c = 0; c < a.mpad && c < a.m; c += 32) {
-    uint32_t r[32];
-    tc::ld_32x32b_x32(t_row + c, r);
-    tc::wait_ld();
-    if (a.epilogue == kSiluMul) {
-      // up rows (64..127) stage bf16(up); gate rows combine
-      if (row >= 64) {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) xs[e * kTileN + 64 + (row - 64)] = __float2bfloat16_rn(__uint_as_float(r[e]));
-      }
-      epi_bar();
-      if (row < 64) {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float g = bf16_round(__uint_as_float(r[e]));
-          const float u = __bfloat162float(xs[e * kTileN + 64 + row]);
-          xs[e * kTileN + row] = __float2bfloat16_rn(silu_mul(g, u));
-        }
-      }
-      epi_bar();
-      store_staged(a, xs, c, tile * 64, 64, et);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 32; ++e) xs[e * kTileN + row] = __float2bfloat16_rn(__uint_as_float(r[e]) + bias);
-      epi_bar();
-      store_staged(a, xs, c, n0, kTileN, et);
-    }
-    epi_bar();
-  }
-}
-
-// The last CTA of a split tile: workspace -> epilogue -> Y, and the workspace
-// back to zero.  Thread et owns workspace row n0 + et (its tokens contiguous);
-// sixteen 16-byte loads are in flight before the first is used.
-__device__ void finish_split_tile(const GemmArgs& a, int tile, int et) {
-  const int n0 = tile * kTileN;
-  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (a.epilogue == kSiluMul) {
-    if (et >= 64) return;  // gate thread et also takes up row et + 64
-    float* g = a.ws + static_cast<int64_t>(n0 + et) * a.ldws;
-    float* u = g + 64 * static_cast<int64_t>(a.ldws);
-    __nv_bfloat16* dst = a.y + tile * 64 + et;
-    for (int c0 = 0; c0 < a.ldws; c0 += 32) {
-      float4 gv[8], uv[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (c0 + 4 * q < a.ldws) {
-          gv[q] = __ldcg(reinterpret_cast<const float4*>(g + c0 + 4 * q));
-          uv[q] = __ldcg(reinterpret_cast<const float4*>(u + c0 + 4 * q));
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (c0 + 4 * q < a.ldws) {
-          __stcg(reinterpret_cast<float4*>(g + c0 + 4 * q), zero);
-          __stcg(reinterpret_cast<float4*>(u + c0 + 4 * q), zero);
-          const float gg[4] = {gv[q].x, gv[q].y, gv[q].z, gv[q].w};
-          const float uu[4] = {uv[q].x, uv[q].y, uv[q].z, uv[q].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int m = c0 + 4 * q + e;
-            if (m < a.m)
-              dst[static_cast<int64_t>(m) * a.ldy] = __float2bfloat16_rn(silu_mul(bf16_round(gg[e]), bf16_round(uu[e])));
-          }
-        }
-      }
-    }
-  } else {
-    float* src = a.ws + static_cast<int64_t>(n0 + et) * a.ldws;
-    const float bias = a.epilogue == kBias ? __bfloat162float(a.bias[n0 + et]) : 0.f;
-    __nv_bfloat16* dst = a.y + n0 + et;
-    for (int c0 = 0; c0 < a.ldws; c0 += 64) {
-      float4 v[16];
-#pragma unroll
-      for (int q = 0; q < 16; ++q)
-        if (c0 + 4 * q < a.ldws) v[q] = __ldcg(reinterpret_cast<const float4*>(src + c0 + 4 * q));
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        if (c0 + 4 * q < a.ldws) {
-          __stcg(reinterpret_cast<float4*>(src + c0 + 4 * q), zero);
-          const float vv[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int m = c0 + 4 * q + e;
-            if (m < a.m) dst[static_cast<int64_t>(m) * a.ldy] = __float2bfloat16_rn(vv[e] + bias);
-          }
-        }
-      }
-    }
-  }
-}
 
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap xmap, GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int ST = a.stages;
-  const int sb = stage_bytes(a.mpad);
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + ST * sb);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * sb + kXsBytes);
+  const int G = a.group;
+  const int sb = stage_bytes(a.mpad, G);
+  const int xoff = G * kWBytes;  // X slabs after the stage's W units
+  const int S = gridDim.y;
+  const int own = a.own;  // tokens per owner CTA (padded to 4)
+  const int ring = ring_bytes(a.mpad, G, a.m, S, ST);
+  float* park = reinterpret_cast<float*>(smem);           // [S * own tokens][128 rows], over the drained ring
+  // [S senders][own tokens][128 rows]; a CTA alone reads its park directly
+  float* recv = S > 1 ? reinterpret_cast<float*>(smem + ring) : park;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring + recv_bytes(a.m, S));
   uint64_t* empty = full + ST;
-  uint64_t* done = empty + ST;  // [2] accumulator b complete
-  uint64_t* tfree = done + 2;   // [2] accumulator b drained by the epilogue
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfree + 2);
-  int* s_last = reinterpret_cast<int*>(tmem_slot + 1);
+  uint64_t* done = empty + ST;   // the accumulator is complete
+  uint64_t* recv_bar = done + 1; // every sender's slice of this CTA's tokens has landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = gridDim.x;
-  const int u0 = first_unit(blockIdx.x, a.units, G);
-  const int u1 = first_unit(blockIdx.x + 1, a.units, G);
-  const int nu = u1 - u0;
+  const int tile = blockIdx.x;
+  const int rank = static_cast<int>(cluster_rank());  // == blockIdx.y: cluster dims (1, S, 1)
+  const int kb0 = rank * a.kbt / S, kb1 = (rank + 1) * a.kbt / S;
+  const int nu = kb1 - kb0;           // >= 1: S <= kbt
+  const int nl = (nu + G - 1) / G;     // stage loads
+  const uint8_t* wsrc = a.wpack + (static_cast<int64_t>(tile) * a.kbt + kb0) * kWBytes;
   uint32_t tmem_cols = 32;
-  while (tmem_cols < static_cast<uint32_t>(2 * a.mpad)) tmem_cols <<= 1;
+  while (tmem_cols < static_cast<uint32_t>(a.mpad)) tmem_cols <<= 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&done[b], 1);
-      mbar_init(&tfree[b], 4);
-    }
+    mbar_init(done, 1);
+    mbar_init(recv_bar, 1);
     fence_barrier_init();
-    // W does not depend on the previous kernel: start streaming it at once
-    const int pro = nu < ST ? nu : ST;
-    for (int j = 0; j < pro; ++j) {
-      mbar_arrive_expect_tx(&full[j], sb);
-      bulk_load(smem + j * sb, a.wpack + static_cast<int64_t>(u0 + j) * kWBytes, kWBytes, &full[j]);
+    // the one arrival on recv_bar; the peers' copies complete its transaction count
+    if (S > 1) mbar_arrive_expect_tx(recv_bar, static_cast<uint32_t>(recv_bytes(a.m, S)));
+    // W does not depend on the previous kernel: start streaming it at once; X (the previous
+    // kernel's output) once that kernel has completed.  Load i carries units [i G, i G + g) of the
+    // slice; its X box always holds G slabs (past the slice: unused, past K: zero fill).
+    const int pro = nl < ST ? nl : ST;
+    for (int i = 0; i < pro; ++i) {
+      const int g = nu - i * G < G ? nu - i * G : G;
+      mbar_arrive_expect_tx(&full[i], g * kWBytes + G * x_bytes(a.mpad));
+      bulk_load(smem + i * sb, wsrc + static_cast<int64_t>(i) * G * kWBytes, g * kWBytes, &full[i]);
     }
+    prefetch_tensormap(&xmap);
+    grid_dependency_wait();
+    for (int i = 0; i < pro; ++i) tma_load_x(smem + i * sb + xoff, &xmap, &full[i], kb0 + i * G);
   }
-  // barrier 2: the mbarrier initialisation (warp 0 arrives without waiting) and the TMEM address
-  // (allocated by warp 1) reach warps 1-5; the producer never waits for the allocation
-  if (warp == 0) {
-    __syncwarp();
-    asm volatile("bar.arrive 2, %0;" ::"n"(kThreads) : "memory");
-  } else {
-    if (warp == 1) {
-      tc::tmem_alloc(tmem_slot, tmem_cols);
-      tc::tmem_relinquish();
-    }
-    tc::fence_before_sync();
-    asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");
-    tc::fence_after_sync();
+  // the next kernel may be scheduled now and stream its own weights while this one finishes
+  grid_dependents_launch();
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, tmem_cols);
+    tc::tmem_relinquish();
   }
-  const uint32_t tmem = warp == 0 ? 0u : *tmem_slot;
+  tc::fence_before_sync();
+  __syncthreads();  // also orders every thread after thread 0's dependency wait (Y may be written)
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  cluster_arrive();  // this CTA's barriers are initialised and recv_bar armed (release)
+  bool ok = true;
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
-    if (lane == 0 && nu > 0) {
-      prefetch_tensormap(&xmap);
-      const int pro = nu < ST ? nu : ST;
-      grid_dependency_wait();
-      for (int j = 0; j < pro; ++j)
-        tma_load_2d(smem + j * sb + kWBytes, &xmap, &full[j], ((u0 + j) % a.kbt) * kBlockK, 0);
-      int issued = pro;
-      for (int j = pro; j < nu; ++j) {
-        const int s = j % ST;
-        if (!mbar_wait(&empty[s], ((j / ST) - 1) & 1, a.status)) break;
-        mbar_arrive_expect_tx(&full[s], sb);
-        bulk_load(smem + s * sb, a.wpack + static_cast<int64_t>(u0 + j) * kWBytes, kWBytes, &full[s]);
-        tma_load_2d(smem + s * sb + kWBytes, &xmap, &full[s], ((u0 + j) % a.kbt) * kBlockK, 0);
-        issued = j + 1;
+    if (lane == 0) {
+      const int pro = nl < ST ? nl : ST;  // issued with the barrier initialisation
+      for (int i = pro; i < nl && ok; ++i) {
+        const int s = i % ST;
+        if (!mbar_wait(&empty[s], ((i / ST) - 1) & 1, a.status)) {
+          ok = false;
+          break;
+        }
+        const int g = nu - i * G < G ? nu - i * G : G;
+        mbar_arrive_expect_tx(&full[s], g * kWBytes + G * x_bytes(a.mpad));
+        bulk_load(smem + s * sb, wsrc + static_cast<int64_t>(i) * G * kWBytes, g * kWBytes, &full[s]);
+        tma_load_x(smem + s * sb + xoff, &xmap, &full[s], kb0 + i * G);
       }
-      // every copy issued has landed before the CTA leaves (bounded)
-      for (int j = issued > ST ? issued - ST : 0; j < issued; ++j) mbar_wait(&full[j % ST], (j / ST) & 1, a.status);
     }
+    cluster_wait();
+    cluster_arrive_relaxed();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = tc::idesc_bf16_f32(kTileN, a.mpad, false, false);
-      int j = 0, seg = 0;
-      bool ok = true;
-      for (int u = u0; u < u1 && ok; ++seg) {
-        const int tile = u / a.kbt;
-        const int seg_end = min(u1, (tile + 1) * a.kbt);
-        const int b = seg & 1;
-        if (seg >= 2 && !mbar_wait(&tfree[b], ((seg - 2) >> 1) & 1, a.status)) break;
+      for (int i = 0; i < nl; ++i) {
+        const int s = i % ST;
+        if (!mbar_wait(&full[s], (i / ST) & 1, a.status)) {
+          ok = false;
+          break;
+        }
         tc::fence_after_sync();
-        const uint32_t acc = tmem + b * a.mpad;
-        const int seg_begin = u;
-        for (; u < seg_end; ++u, ++j) {
-          const int s = j % ST;
-          if (!mbar_wait(&full[s], (j / ST) & 1, a.status)) {
-            ok = false;
-            break;
-          }
-          tc::fence_after_sync();
-          const uint32_t w_addr = smem_addr(smem + s * sb);
-          const uint32_t x_addr = w_addr + kWBytes;
+        const int g = nu - i * G < G ? nu - i * G : G;
+        for (int u = 0; u < g; ++u) {
+          const uint32_t w_addr = smem_addr(smem + s * sb + u * kWBytes);
+          const uint32_t x_addr = smem_addr(smem + s * sb + xoff + u * x_bytes(a.mpad));
 #pragma unroll
           for (int kk = 0; kk < kBlockK / 16; ++kk) {
             const uint64_t da = tc::smem_desc_sw128(w_addr + kk * 32, 16, 1024);
             const uint64_t db = tc::smem_desc_sw128(x_addr + kk * 32, 16, 1024);
-            tc::mma_f16_ss(acc, da, db, idesc, (u > seg_begin || kk > 0) ? 1u : 0u);
+            tc::mma_f16_ss(tmem, da, db, idesc, (i > 0 || u > 0 || kk > 0) ? 1u : 0u);
           }
-          tc::commit(&empty[s]);
         }
-        tc::commit(&done[b]);  // arrives once every MMA above has completed
+        tc::commit(&empty[s]);
       }
+      tc::commit(done);  // arrives once every MMA above has completed
     }
+    cluster_wait();
+    cluster_arrive_relaxed();
   } else {
-    // ---------------------------------------------------------------- epilogue warps
-    grid_dependency_wait();
-    const int et = threadIdx.x - 64;  // 0..127
+    // ---------------------------------------------------------------- epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // tile row = TMEM lane
-    int seg = 0;
-    for (int u = u0; u < u1; ++seg) {
-      const int tile = u / a.kbt;
-      const int seg_end = min(u1, (tile + 1) * a.kbt);
-      const int b = seg & 1;
-      const bool done_ok = mbar_wait(&done[b], (seg >> 1) & 1, a.status);
-      tc::fence_after_sync();
-      const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + b * a.mpad;
-      const int c_first = cta_of(tile * a.kbt, a.units, G);
-      const int c_last = cta_of((tile + 1) * a.kbt - 1, a.units, G);
-      if (c_first == c_last) {
-        if (done_ok) direct_epilogue(a, t_row, row, tile, xs, et);
-      } else {
-        // partial sum of a shared tile: 16-byte fp32 reductions into workspace row n0 + row, then the ticket
-        float* ws_row = a.ws + static_cast<int64_t>(tile * kTileN + row) * a.ldws;
-        for (int c = 0; c < a.mpad && c < a.m; c += 32) {
-          uint32_t r[32];
-          tc::ld_32x32b_x32(t_row + c, r);
-          tc::wait_ld();
+    ok = mbar_wait(done, 0, a.status);
+    tc::fence_after_sync();
+    cluster_wait();  // every peer's recv_bar is armed
+    // park the partial token-major: park[tok][row] (conflict-free), zeros past the accumulator
+    const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int padded = S * own;
+    for (int c = 0; c < padded; c += 64) {  // two 32-column TMEM loads in flight per wait
+      uint32_t r[2][32];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            if (c + 4 * q < a.m && done_ok) {
-              red_add_v4(ws_row + c + 4 * q, __uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                         __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-            }
+      for (int h = 0; h < 2; ++h)
+        if (c + 32 * h < padded && c + 32 * h < static_cast<int>(tmem_cols)) tc::ld_32x32b_x32(t_row + c + 32 * h, r[h]);
+      tc::wait_ld();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const bool have = c + 32 * h < static_cast<int>(tmem_cols) && ok;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int tok = c + 32 * h + e;
+          if (tok < padded) park[tok * kTileN + row] = have ? __uint_as_float(r[h][e]) : 0.f;
+        }
+      }
+    }
+    fence_proxy_async_smem();  // the parked partial is read by the bulk copies (async proxy)
+    epi_bar();
+    cluster_wait();  // every peer's recv_bar is armed
+    if (threadIdx.x == 64 && S > 1) {
+      // owner o gets tokens [o * own, o * own + own) of this partial in its slot [rank]
+      const uint32_t slice = static_cast<uint32_t>(own * kTileN * 4);
+      const uint32_t dst = smem_addr(recv) + static_cast<uint32_t>(rank) * slice;
+      const uint32_t bar = smem_addr(recv_bar);
+      for (int o = 0; o < S; ++o)
+        bulk_copy_to_peer(map_rank(dst, o), park + o * own * kTileN, slice, map_rank(bar, o));
+    }
+    // receive this CTA's tokens [rank * own, rank * own + own) from every sender, sum, epilogue, store
+    const bool got = S == 1 || mbar_wait(recv_bar, 0, a.status);
+    cluster_arrive_relaxed();  // everything addressed to this CTA has landed (its sources are read)
+    const int t0 = rank * own;
+    const int nt = a.m - t0 < own ? a.m - t0 : own;
+    // sums from shared memory (4 tokens' loads in flight), bf16 stores coalesced along the tile's rows
+    const float* __restrict__ in = recv + row;
+    __nv_bfloat16* __restrict__ out = a.y;
+    const bool silu = a.epilogue == kSiluMul;
+    const int col = silu ? tile * 64 + row : tile * kTileN + row;
+    const float bias = a.epilogue == kBias ? __bfloat162float(a.bias[tile * kTileN + row]) : 0.f;
+    if (!silu || row < 64) {
+      for (int t = 0; t < nt; t += 4) {
+        float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int s2 = 0; s2 < S; ++s2) {
+          float gv[4], uv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int tt = t + e < nt ? t + e : t;
+            gv[e] = in[(s2 * own + tt) * kTileN];
+            uv[e] = silu ? in[(s2 * own + tt) * kTileN + 64] : 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) g[e] += gv[e], u[e] += uv[e];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (t + e < nt && got) {
+            const float v = silu ? silu_mul(bf16_round(g[e]), bf16_round(u[e])) : g[e] + bias;
+            out[static_cast<int64_t>(t0 + t + e) * a.ldy + col] = __float2bfloat16_rn(v);
           }
         }
-        __threadfence();
-        epi_bar();
-        if (et == 0) {
-          const int arrived = atomicAdd(&a.ticket[tile], 1);
-          const bool last = arrived == c_last - c_first;
-          if (last) a.ticket[tile] = 0;
-          *s_last = last ? 1 : 0;
-        }
-        epi_bar();
-        if (*s_last) {
-          __threadfence();
-          finish_split_tile(a, tile, et);
-        }
-        epi_bar();
       }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tfree[b]);
-      u = seg_end;
     }
   }
+  // every CTA has received all it was sent: no store of this CTA is still in flight when it leaves
+  cluster_wait();
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 1) {
@@ -439,49 +371,62 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 
 // 2-D K-major map of a row-major bf16 matrix [rows, cols] with leading dimension ld, box {64, box_rows}.
-int encode_2d(CUtensorMap* map, const void* base, int rows, int cols, int64_t ld, int box_rows) {
+// X [rows, cols] (row pitch ld) viewed as {64 k, rows, cols / 64 slabs} with box {64, box_rows, group}: one
+// copy brings `group` K slabs, each [box_rows x 128 B] with the 128-byte swizzle, one after another.
+int encode_x(CUtensorMap* map, const void* base, int rows, int cols, int64_t ld, int box_rows, int group) {
   auto encode = get_encode();
   if (encode == nullptr) return NQT_ERR_CUDA;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kBlockK), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(cols / kBlockK)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(kBlockK) * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(box_rows),
+                       static_cast<cuuint32_t>(group)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? NQT_OK : NQT_ERR_CUDA;
 }
 
-int smem_bytes(int mpad, int stages) {
-  return 1024 + stages * stage_bytes(mpad) + kXsBytes + (2 * stages + 4) * 8 + 16;
+int smem_bytes(int mpad, int group, int m, int S, int stages) {
+  return 1024 + ring_bytes(mpad, group, m, S, stages) + recv_bytes(m, S) + (2 * stages + 2) * 8 + 16;
 }
 
-struct Workspace {
-  float* ws = nullptr;
-  int* ticket = nullptr;
-};
-
-// Per-device addresses of the static workspace (looked up once per device).
-int workspace(Workspace* out) {
+// Clusters of S CTAs with `smem` bytes each that the current device holds at once (cached).
+int max_active_clusters(int S, int smem) {
   static std::mutex mu;
-  static Workspace cache[64];
-  static bool have[64] = {};
+  static int dev_cached = -1;
+  static int cache[kMaxSplit + 1][64] = {};  // [S][smem in 4 KB steps]
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NQT_ERR_CUDA;
+  cudaGetDevice(&dev);
+  const int bucket = smem / 4096 < 64 ? smem / 4096 : 63;
   std::lock_guard<std::mutex> lock(mu);
-  if (!have[dev]) {
-    void* p = nullptr;
-    void* q = nullptr;
-    if (cudaGetSymbolAddress(&p, g_ws) != cudaSuccess || cudaGetSymbolAddress(&q, g_ws_ticket) != cudaSuccess) {
-      set_last_message("gemm: workspace symbol lookup failed");
-      return NQT_ERR_CUDA;
-    }
-    cache[dev].ws = static_cast<float*>(p);
-    cache[dev].ticket = static_cast<int*>(q);
-    have[dev] = true;
+  if (dev != dev_cached) {
+    for (auto& row : cache)
+      for (int& v : row) v = 0;
+    dev_cached = dev;
   }
-  *out = cache[dev];
-  return NQT_OK;
+  int& v = cache[S][bucket];
+  if (v == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, S, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = S;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel, &cfg) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = 1 << 20;  // unknown: do not shrink the split
+    }
+    v = n;
+  }
+  return v;
 }
 
 }  // namespace
@@ -503,12 +448,13 @@ extern "C" int nqt_gemm_pack_weight(const void* w, int64_t ldw, int n, int k, in
 }
 
 extern "C" int nqt_gemm_bf16(const void* x, int64_t ldx, const void* wpacked, void* y, int64_t ldy,
-                             const void* bias, int m, int n, int k, int epilogue, int ctas, int32_t* status,
+                             const void* bias, int m, int n, int k, int epilogue, int split, int32_t* status,
                              void* stream) {
   if (!x || !wpacked || !y) return NQT_ERR_ARG;
   if (m < 1 || m > 256 || n < kTileN || k < kBlockK) return NQT_ERR_ARG;
   if (n % kTileN != 0 || k % kBlockK != 0) return NQT_ERR_UNSUPPORTED;
   if (epilogue < kPlain || epilogue > kSiluMul || (epilogue == kBias && bias == nullptr)) return NQT_ERR_ARG;
+  if (split < 0 || split > kMaxSplit) return NQT_ERR_ARG;
   // TMA / bulk copies: 16-byte aligned bases and row pitches
   if ((reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(wpacked) & 15u) || (ldx * 2) % 16 ||
       ldx < k)
@@ -516,43 +462,77 @@ extern "C" int nqt_gemm_bf16(const void* x, int64_t ldx, const void* wpacked, vo
   const int out_cols = epilogue == kSiluMul ? n / 2 : n;
   if (ldy < out_cols) return NQT_ERR_ARG;
   const int tiles = n / kTileN;
-  const int ldws = (m + 3) / 4 * 4;
-  if (tiles > kMaxTiles || static_cast<int64_t>(ldws) * n > kMaxWsFloats) return NQT_ERR_CAPACITY;
+  if (tiles > 65535) return NQT_ERR_UNSUPPORTED;
   const int mpad = (m + 15) / 16 * 16;
   const int kbt = k / kBlockK;
-  const int units = tiles * kbt;
-  // one CTA per SM (the shared-memory ring keeps it so), never more CTAs than units
-  if (ctas <= 0) ctas = num_sms();
-  if (ctas > units) ctas = units;
-  int stages = 8;
-  while (stages > 2 && smem_bytes(mpad, stages) > 227 * 1024) --stages;
-  const int smem = smem_bytes(mpad, stages);
-  if (smem > 227 * 1024) return NQT_ERR_UNSUPPORTED;
-  Workspace wsp;
-  if (workspace(&wsp) != NQT_OK) return NQT_ERR_CUDA;
+  // K split = cluster size: the largest power of two (<= 8, <= K units per tile) that keeps the grid
+  // within one CTA per SM and within the clusters the GPU can hold at once
+  int S = split;
+  if (S == 0) {
+    S = 1;
+    while (S * 2 <= kMaxSplit && S * 2 <= kbt && tiles * S * 2 <= num_sms()) S *= 2;
+  }
+  if (S > kbt) S = kbt;
+  // TMEM holds 512 columns per SM.  A CTA blocked in tcgen05.alloc while its cluster peers wait at the
+  // cluster barrier would deadlock, so shared memory is padded until no SM can hold more CTAs than
+  // their columns fit: at least cols/512 of the SM's 228 KB, plus the 1 KB the runtime reserves per CTA.
+  int tmem_cols = 32;
+  while (tmem_cols < mpad) tmem_cols <<= 1;
+  const int tmem_floor = tmem_cols * (233472 / 512);
+  // per split: K units per stage (up to kMaxGroup: few, large copies), then as many stages as fit
+  struct Plan {
+    int group, stages, smem;
+  };
+  auto plan_for = [&](int s_split) {
+    Plan pl;
+    const int per_cta = (kbt + s_split - 1) / s_split;  // K units of the longest slice
+    pl.group = per_cta < kMaxGroup ? per_cta : kMaxGroup;
+    // keep two stages in flight when the slice has two loads' worth (a lone stage serialises copy and MMA)
+    const int want = per_cta > pl.group ? 2 : 1;
+    while (pl.group > 1 && smem_bytes(mpad, pl.group, m, s_split, want) > kSmemBudget) --pl.group;
+    const int loads = (per_cta + pl.group - 1) / pl.group;
+    pl.stages = loads < kMaxStages ? loads : kMaxStages;
+    while (pl.stages > 1 && smem_bytes(mpad, pl.group, m, s_split, pl.stages) > kSmemBudget) --pl.stages;
+    const int sm = smem_bytes(mpad, pl.group, m, s_split, pl.stages);
+    pl.smem = sm > tmem_floor ? sm : tmem_floor;
+    return pl;
+  };
+  // a split whose park and receive buffers do not fit beside one stage runs unsplit
+  if (plan_for(S).smem > kSmemBudget) S = 1;
+  Plan pl = plan_for(S);
+  if (pl.smem > kSmemBudget) return NQT_ERR_UNSUPPORTED;
+  static std::once_flag once;
+  std::call_once(once,
+                 [] { cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget); });
+  // an automatic split whose clusters do not all fit at once runs a second wave: halve it until they do
+  while (split == 0 && S > 1 && tiles > max_active_clusters(S, pl.smem)) {
+    S /= 2;
+    pl = plan_for(S);
+    if (pl.smem > kSmemBudget) return NQT_ERR_UNSUPPORTED;
+  }
 
   CUtensorMap xmap;
-  if (encode_2d(&xmap, x, m, k, ldx, mpad) != NQT_OK) {
+  if (encode_x(&xmap, x, m, k, ldx, mpad, pl.group) != NQT_OK) {
     set_last_message("gemm: cuTensorMapEncodeTiled failed");
     return NQT_ERR_CUDA;
   }
-  const int vec_out = (reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy * 2) % 16 == 0;
   GemmArgs a{static_cast<const uint8_t*>(wpacked), static_cast<__nv_bfloat16*>(y), ldy,
-             static_cast<const __nv_bfloat16*>(bias), status, wsp.ws, wsp.ticket, m, n, k, mpad, epilogue, stages,
-             kbt, units, vec_out, ldws};
-  static std::once_flag once;
-  std::call_once(once,
-                 [] { cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024); });
+             static_cast<const __nv_bfloat16*>(bias), status, m, n, k, mpad, epilogue, pl.stages, kbt,
+             own_tokens(m, S), pl.group};
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(ctas, 1, 1);
+  cfg.gridDim = dim3(tiles, S, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = as_stream(stream);
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  attrs[1].id = cudaLaunchAttributeClusterDimension;
+  attrs[1].val.clusterDim.x = 1;
+  attrs[1].val.clusterDim.y = S;
+  attrs[1].val.clusterDim.z = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, gemm_kernel, xmap, a);
   if (err != cudaSuccess) {
     set_last_error("gemm", err);

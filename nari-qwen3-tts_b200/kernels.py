@@ -370,10 +370,11 @@ class PackedWeight:
 
 def linear(x: torch.Tensor, weight: PackedWeight, bias: torch.Tensor | None = None, *,
            out: torch.Tensor | None = None, split: int = 0) -> torch.Tensor:
-    # split: CTAs of the stream-K grid (0 = one per SM)
     """x [m, k] @ W[n, k]^T (+ bias) on the weight-streaming tcgen05 GEMM
     (the decoder projections, model/layers.py:195-270).  A ``gate_up`` packed
-    weight gives silu(gate) * up, [m, n / 2]."""
+    weight gives silu(gate) * up, [m, n / 2].  ``split``: CTAs (one cluster)
+    sharing each 128-row tile's K, 1..8; 0 picks the largest that keeps the
+    grid within one CTA per SM."""
 
     if not isinstance(weight, PackedWeight):
         raise TypeError("linear takes a PackedWeight")

@@ -48,19 +48,27 @@ def test_plain_matches_fp32_reference(nqt, cuda, m, n, k):
     assert nqt.kernels.read_status(cuda) == 0
 
 
-@pytest.mark.parametrize("ctas", [1, 3, 8, 37, 148, 256])
-def test_every_stream_k_partition_gives_the_same_result(nqt, cuda, ctas):
-    # tiles written by one CTA, tiles shared by 2..n CTAs (workspace + ticket), several tiles per CTA
+@pytest.mark.parametrize("split", [1, 2, 3, 5, 8])
+def test_every_k_split_gives_the_same_result(nqt, cuda, split):
+    # one CTA per tile, and clusters of 2..8 CTAs splitting K (uneven slices at 3 and 5) reduced
+    # through distributed shared memory; called twice: nothing carries over between calls
     g = torch.Generator(device=cuda).manual_seed(11)
     x = torch.randn(64, 2048, generator=g, device=cuda).to(torch.bfloat16)
     w = (torch.randn(1024, 2048, generator=g, device=cuda) * 2048 ** -0.5).to(torch.bfloat16)
     pw = nqt.kernels.PackedWeight(w)
     want = _ref(x, w)
-    for _ in range(2):  # the second call sees the workspace zeroed again by the first
-        y = nqt.kernels.linear(x, pw, split=ctas)
+    for _ in range(2):
+        y = nqt.kernels.linear(x, pw, split=split)
         torch.cuda.synchronize()
         _close(y, want)
     assert nqt.kernels.read_status(cuda) == 0
+
+
+def test_split_beyond_the_cluster_limit_is_rejected(nqt, cuda):
+    x = torch.randn(64, 512, device=cuda).to(torch.bfloat16)
+    pw = nqt.kernels.PackedWeight((torch.randn(256, 512, device=cuda) * 0.05).to(torch.bfloat16))
+    with pytest.raises(nqt.NqtError):
+        nqt.kernels.linear(x, pw, split=9)
 
 
 def test_bias_epilogue(nqt, cuda):
