@@ -701,8 +701,8 @@ def main() -> None:
     peak, peak_kind = peaks()
     achieved = attn_bytes / (attn_ms / 1e3) / 1e9
     # DRAM traffic of one decode launch from an ncu capture of this kernel on the same contexts
-    # (2-layer model, Sum(ctx + 2) = 74466 tokens): 307.57 MB read + 4.90 MB written, scaled by tokens
-    traffic = (307.566080e6 + 4.895232e6) * (sum(lengths) / 74466.0) if args.layers == 28 else None
+    # (2-layer model, Sum(ctx + 2) = 74466 tokens): 307.88 MB read + 4.19 MB written, scaled by tokens
+    traffic = (307.876352e6 + 4.194816e6) * (sum(lengths) / 74466.0) if args.layers == 28 else None
     status = nqt.kernels.read_status(dev) | int(step.planner.status.item())
 
     line = {
