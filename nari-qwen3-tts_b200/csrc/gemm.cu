@@ -75,7 +75,8 @@ struct GemmArgs {
   int stages;
   int kbt;    // K units per tile
   int own;    // tokens per cluster rank, own_tokens(m, S)
-  int group;  // K units per stage (one W bulk copy, one X tensor load)
+  int group;    // K units per stage (one W bulk copy, one X tensor load)
+  int vec_out;  // y and its row pitch 8-byte aligned: 4-column vector stores
 };
 
 __host__ __device__ constexpr int x_bytes(int mpad) { return mpad * kBlockK * 2; }
@@ -116,12 +117,20 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   return r;
 }
 
-// Cluster barrier, split: every thread of every CTA arrives, then waits (release / acquire at cluster scope).
-__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+// Cluster barrier, split: every thread of every CTA arrives once, then waits once (release / acquire at
+// cluster scope), alternating.  Whole converged warps only (.aligned): call sites reconverge first.
+__device__ __forceinline__ void cluster_arrive() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  __syncwarp();
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 // Contiguous copy from this CTA's shared memory into a peer's, completing `bar_cluster_addr`'s
 // transaction count there (16-byte aligned, size % 16 == 0).
@@ -140,6 +149,12 @@ __device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
+}
+
+__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + __expf(-g)) * u; }
@@ -263,7 +278,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const int row = quarter * 32 + lane;  // tile row = TMEM lane
     ok = mbar_wait(done, 0, a.status);
     tc::fence_after_sync();
-    cluster_wait();  // every peer's recv_bar is armed
     // park the partial token-major: park[tok][row] (conflict-free), zeros past the accumulator
     const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const int padded = S * own;
@@ -299,32 +313,70 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     cluster_arrive_relaxed();  // everything addressed to this CTA has landed (its sources are read)
     const int t0 = rank * own;
     const int nt = a.m - t0 < own ? a.m - t0 : own;
-    // sums from shared memory (4 tokens' loads in flight), bf16 stores coalesced along the tile's rows
-    const float* __restrict__ in = recv + row;
-    __nv_bfloat16* __restrict__ out = a.y;
     const bool silu = a.epilogue == kSiluMul;
-    const int col = silu ? tile * 64 + row : tile * kTileN + row;
-    const float bias = a.epilogue == kBias ? __bfloat162float(a.bias[tile * kTileN + row]) : 0.f;
-    if (!silu || row < 64) {
-      for (int t = 0; t < nt; t += 4) {
-        float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int s2 = 0; s2 < S; ++s2) {
-          float gv[4], uv[4];
+    // thread = one fixed quad of 4 tile rows (silu: 4 gate rows and their up rows) and every
+    // (128 / quads)-th token; four tokens per pass as independent load -> sum -> store chains (one
+    // warp per scheduler has nothing else to hide their latency behind)
+    const uint32_t recv_s = smem_addr(recv);
+    const uint32_t slice_stride = static_cast<uint32_t>(own * kTileN * 4);  // bytes between senders
+    const int quads = silu ? 16 : 32;
+    const int q = row % quads;
+    const int tstep = kTileN / quads;  // tokens covered by one pass of the 128 threads
+    const int col = silu ? tile * 64 + 4 * q : tile * kTileN + 4 * q;
+    float4 bias4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (a.epilogue == kBias) {
+      bias4.x = __bfloat162float(a.bias[col]);
+      bias4.y = __bfloat162float(a.bias[col + 1]);
+      bias4.z = __bfloat162float(a.bias[col + 2]);
+      bias4.w = __bfloat162float(a.bias[col + 3]);
+    }
+    __nv_bfloat16* const ybase = a.y + col;
+    const int64_t ldy = a.ldy;
+    const bool vec = a.vec_out != 0;
+    for (int tb = row / quads; tb < nt; tb += 4 * tstep) {
+      float4 g[4], u[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int tt = t + e < nt ? t + e : t;
-            gv[e] = in[(s2 * own + tt) * kTileN];
-            uv[e] = silu ? in[(s2 * own + tt) * kTileN + 64] : 0.f;
+      for (int k = 0; k < 4; ++k) g[k] = u[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s2 = 0; s2 < S; ++s2) {
+        const uint32_t base = recv_s + s2 * slice_stride + static_cast<uint32_t>((tb * kTileN + 4 * q) * 4);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (tb + k * tstep < nt) {
+            const uint32_t src = base + static_cast<uint32_t>(k * tstep * kTileN * 4);
+            const float4 gv = ld_shared_v4(src);
+            g[k].x += gv.x, g[k].y += gv.y, g[k].z += gv.z, g[k].w += gv.w;
+            if (silu) {
+              const float4 uv = ld_shared_v4(src + 64 * 4);
+              u[k].x += uv.x, u[k].y += uv.y, u[k].z += uv.z, u[k].w += uv.w;
+            }
           }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) g[e] += gv[e], u[e] += uv[e];
         }
+      }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (t + e < nt && got) {
-            const float v = silu ? silu_mul(bf16_round(g[e]), bf16_round(u[e])) : g[e] + bias;
-            out[static_cast<int64_t>(t0 + t + e) * a.ldy + col] = __float2bfloat16_rn(v);
-          }
+      for (int k = 0; k < 4; ++k) {
+        const int t = tb + k * tstep;
+        if (t >= nt || !got) continue;
+        float v0, v1, v2, v3;
+        if (silu) {
+          v0 = silu_mul(bf16_round(g[k].x), bf16_round(u[k].x));
+          v1 = silu_mul(bf16_round(g[k].y), bf16_round(u[k].y));
+          v2 = silu_mul(bf16_round(g[k].z), bf16_round(u[k].z));
+          v3 = silu_mul(bf16_round(g[k].w), bf16_round(u[k].w));
+        } else {
+          v0 = g[k].x + bias4.x, v1 = g[k].y + bias4.y, v2 = g[k].z + bias4.z, v3 = g[k].w + bias4.w;
+        }
+        __nv_bfloat16* dst = ybase + static_cast<int64_t>(t0 + t) * ldy;
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(v0, v1), hi = __floats2bfloat162_rn(v2, v3);
+        if (vec) {
+          uint2 pk;
+          pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+          pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(dst) = pk;
+        } else {
+          dst[0] = lo.x;
+          dst[1] = lo.y;
+          dst[2] = hi.x;
+          dst[3] = hi.y;
         }
       }
     }
@@ -518,7 +570,8 @@ extern "C" int nqt_gemm_bf16(const void* x, int64_t ldx, const void* wpacked, vo
   }
   GemmArgs a{static_cast<const uint8_t*>(wpacked), static_cast<__nv_bfloat16*>(y), ldy,
              static_cast<const __nv_bfloat16*>(bias), status, m, n, k, mpad, epilogue, pl.stages, kbt,
-             own_tokens(m, S), pl.group};
+             own_tokens(m, S), pl.group,
+             (reinterpret_cast<uintptr_t>(y) & 7u) == 0 && ldy % 4 == 0 ? 1 : 0};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, S, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
