@@ -142,6 +142,16 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(const int32_t* indptr
 }
 
 // ------------------------------------------------------------------ decode
+// 4-D tiled TMA load with an L2 cache policy (the K/V stream is read once per launch: evict first, so it
+// does not push q, the page table and the partials out of L2).
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                                 int c2, int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
+      : "memory");
+}
 __device__ __forceinline__ int64_t range_start(int64_t total, int c, int n) { return total * c / n; }
 
 // Sequence that owns flat tile t: last b with tile_indptr[b] <= t.
@@ -321,6 +331,8 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
     // Lane l issues box l of each stage (KV head l / kHalves, dims half l % kHalves): one thread
     // issuing every box serialises on the per-instruction TMA issue cost.
     const int box_h = lane / kHalves, box_half = lane % kHalves;
+    uint64_t evict_first;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(evict_first));
     int seq = seq_a;
     int seq_t0 = prefix[seq];
     int seq_t1 = prefix[seq + 1];
@@ -354,8 +366,8 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
       if (lane == 0) mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
       __syncwarp();
       if (lane < HPC * kHalves)
-        tma_load_4d(smem + s * Cfg::kStageBytes + (box_h * kHalves + box_half) * kBoxBytes, &tmap, &full[s],
-                    box_half * 64, kv0 + box_h, tile_in_page * kTok, page * 2);
+        tma_load_4d_hint(smem + s * Cfg::kStageBytes + (box_h * kHalves + box_half) * kBoxBytes, &tmap, &full[s],
+                         box_half * 64, kv0 + box_h, tile_in_page * kTok, page * 2, evict_first);
     }
     return;
   }
