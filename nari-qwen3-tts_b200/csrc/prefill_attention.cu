@@ -54,6 +54,70 @@ struct PrefillCfg {
 
 __device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory"); }
 
+// (sequence, query tile) of CTA `cta`, longest first (called by a whole warp; every lane gets the
+// result; seq = -1: no tile).  A query tile's cost is the number of 64-key blocks up to its diagonal,
+// nb = ceil(e / 64) with e = min(kv_len, shift + (i + 1) * tpt) the key end of tile i (shift = kv_len -
+// qo_len), non-decreasing in i.  CTAs take tiles in decreasing nb (ties: batch order, then tile
+// order), so the first wave starts the most expensive tiles of every chunk and the cheap ones fill the
+// tail.  For one sequence the tiles with nb >= v are its last ge(v) tiles, ge(v) = T - #{i : e_i <=
+// 64 (v - 1)}, so the CTA's level v is a binary search over sums of ge and its tile a scan over the batch.
+struct SeqTiles {
+  int tiles, shift, kv_len;
+};
+
+__device__ __forceinline__ SeqTiles seq_tiles(const int32_t* qo_indptr, const int32_t* kv_indptr,
+                                              const int32_t* last_len, int page_size, int b, int tpt) {
+  SeqTiles t{0, 0, 0};
+  const int qo = qo_indptr[b + 1] - qo_indptr[b];
+  const int n_pages = kv_indptr[b + 1] - kv_indptr[b];
+  if (qo <= 0 || n_pages <= 0) return t;
+  int ll = last_len[b];
+  ll = ll < 1 ? 1 : (ll > page_size ? page_size : ll);
+  t.kv_len = (n_pages - 1) * page_size + ll;
+  t.shift = t.kv_len - qo;
+  t.tiles = (qo + tpt - 1) / tpt;
+  return t;
+}
+
+constexpr int kStagedSeqs = 512;  // sequences whose tile geometry the mapping keeps in shared memory
+
+__device__ void longest_first_tile(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* last_len,
+                                   int page_size, int batch, int tpt, int cta, int& seq, int& tile) {
+  const int lane = threadIdx.x & 31;
+  __shared__ SeqTiles s_seq[kStagedSeqs];
+  seq = -1;
+  tile = 0;
+  const bool staged = batch <= kStagedSeqs;
+  if (staged) {
+    for (int b = lane; b < batch; b += 32) s_seq[b] = seq_tiles(qo_indptr, kv_indptr, last_len, page_size, b, tpt);
+    __syncwarp();
+  }
+  auto geom = [&](int b) {
+    return staged ? s_seq[b] : seq_tiles(qo_indptr, kv_indptr, last_len, page_size, b, tpt);
+  };
+  // lane-parallel over the batch: the tiles of the sequences ahead of b (longer key length first, ties
+  // in batch order), then the one sequence whose tiles hold this CTA
+  for (int base = 0; base < batch; base += 32) {
+    const int b = base + lane;
+    SeqTiles tb{0, 0, 0};
+    int first = 0;
+    if (b < batch) {
+      tb = geom(b);
+      for (int o = 0; o < batch; ++o) {
+        const SeqTiles to = geom(o);
+        if (to.kv_len > tb.kv_len || (to.kv_len == tb.kv_len && o < b)) first += to.tiles;
+      }
+    }
+    const unsigned hit = __ballot_sync(kFull, tb.tiles > 0 && cta >= first && cta < first + tb.tiles);
+    if (hit != 0u) {
+      const int src = __ffs(hit) - 1;
+      seq = base + src;
+      tile = __shfl_sync(kFull, tb.tiles - 1 - (cta - first), src);  // a sequence's last (longest) tile first
+      return;
+    }
+  }
+}
+
 template <int D, int STAGES>
 __global__ void __launch_bounds__((kConsumers + 1) * 32) prefill_kernel(const __grid_constant__ CUtensorMap tmap,
                                                                         PrefillArgs p) {
@@ -66,23 +130,19 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) prefill_kernel(const __
   int* s_info = reinterpret_cast<int*>(empty + STAGES);
 
   const int kvh = blockIdx.y;
+  const int cta = blockIdx.x;
   const int G = p.group;
   const int tokens_per_tile = kRows / G;
-  if (threadIdx.x == 0) {
-    // locate (sequence, tile) of this CTA
-    int remaining = blockIdx.x, seq = -1, tile = 0;
-    for (int b = 0; b < p.batch; ++b) {
-      const int qo = p.qo_indptr[b + 1] - p.qo_indptr[b];
-      const int tiles = qo > 0 ? (qo + tokens_per_tile - 1) / tokens_per_tile : 0;
-      if (remaining < tiles) {
-        seq = b;
-        tile = remaining;
-        break;
-      }
-      remaining -= tiles;
+  if (threadIdx.x < 32) {
+    int seq, tile;
+    longest_first_tile(p.qo_indptr, p.kv_indptr, p.last_len, p.page_size, p.batch, tokens_per_tile, cta, seq,
+                       tile);
+    if (threadIdx.x == 0) {
+      s_info[0] = seq;
+      s_info[1] = tile;
     }
-    s_info[0] = seq;
-    s_info[1] = tile;
+  }
+  if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers);
@@ -364,22 +424,18 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int kvh = blockIdx.y;
+  const int cta = blockIdx.x;
   const int G = p.group;
   const int tpt = kM / G;
-  if (threadIdx.x == 0) {
-    int remaining = blockIdx.x, seq = -1, tile = 0;
-    for (int b = 0; b < p.batch; ++b) {
-      const int qo = p.qo_indptr[b + 1] - p.qo_indptr[b];
-      const int tiles = qo > 0 ? (qo + tpt - 1) / tpt : 0;
-      if (remaining < tiles) {
-        seq = b;
-        tile = remaining;
-        break;
-      }
-      remaining -= tiles;
+  if (threadIdx.x < 32) {
+    int seq, tile;
+    longest_first_tile(p.qo_indptr, p.kv_indptr, p.last_len, p.page_size, p.batch, tpt, cta, seq, tile);
+    if (threadIdx.x == 0) {
+      info[0] = seq;
+      info[1] = tile;
     }
-    info[0] = seq;
-    info[1] = tile;
+  }
+  if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
