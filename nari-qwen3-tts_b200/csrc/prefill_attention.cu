@@ -374,31 +374,44 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) prefill_kernel(const __
 }
 
 // ------------------------------------------------------------------ tcgen05 path (D = 128)
-// CTA = 128 query rows (token x GQA head) x one KV head; KV blocks of 64 tokens.
-//   warp 0      TMA producer (Q once, then K and V of each block)
-//   warp 1      TMEM allocator and the single MMA-issuing thread
-//   warps 2..5  softmax: thread = one query row = one TMEM lane
-// TMEM columns: S double buffer [0, 64) and [64, 128) (fp32), O [128, 256) (fp32).
-// S = Q K^T: A = Q (K-major, 128B swizzle), B = K (K-major); O += P V: A = P
-// (bf16, written by the softmax threads into a swizzled SMEM tile, K-major),
-// B = V (MN-major: token rows of 64 contiguous dims).  O is rescaled in TMEM
-// only when a row's running max grows by more than 2^8 (exact either way:
-// the exponent base only has to be shared by P and l).
+// CTA = two 128-row query tiles of one sequence and one KV head (row = token x GQA head; tile A holds
+// the first 128 / G tokens, tile B the next 128 / G), over KV blocks of 64 tokens.  Both tiles read
+// every K / V block from the same shared-memory stage, so a CTA moves half the K / V bytes per FLOP
+// of a one-tile CTA: with one tile, the per-SM delivery of the 16-token K / V boxes (about 20 B per
+// cycle), not the tensor pipe or the softmax, set the time per block.
+//   warp 0       TMA producer (Q of both tiles, then K and V of each block)
+//   warp 1       TMEM allocator and the single MMA-issuing thread
+//   warps 2..5   softmax of tile A, warps 6..9 softmax of tile B: thread = one query row = one TMEM lane
+// TMEM (512 columns): tile t has its S double buffer at [128 t, 128 t + 64) and [128 t + 64, 128 t + 128)
+// and O at [256 + 128 t, 384 + 128 t), all fp32.  S = Q K^T: A = Q (K-major, 128B swizzle), B = K
+// (K-major).  P (bf16, two per column) overwrites the first 32 columns of its own S buffer, and
+// O += P V takes A = P from TMEM and B = V (MN-major: token rows of 64 contiguous dims).  O is
+// rescaled in TMEM only when a row's running max grows by more than 2^8 (exact either way: the
+// exponent base only has to be shared by P and l).
 namespace tcp {
-constexpr int kM = 128;
-constexpr int kN = 64;
+constexpr int kM = 128;                  // rows per tile
+constexpr int kTiles = 2;                // tiles per CTA
+constexpr int kN = 64;                   // keys per block
 constexpr int kStages = 4;
-constexpr int kSmemPages = 1024;  // page ids of the sequence staged in shared memory
-constexpr int kQBytes = kM * 128 * 2;           // [half][128 rows][128 B]
-constexpr int kKVHalf = kN * 128;               // [64 tokens][128 B]
-constexpr int kKVBytes = 4 * kKVHalf;           // K h0, K h1, V h0, V h1
-constexpr int kPBytes = kM * kN * 2;            // [128 rows][128 B]
-constexpr int kThreads = 6 * 32;
+constexpr int kSmemPages = 1024;         // page ids of the sequence staged in shared memory
+constexpr int kQBytes = kM * 128 * 2;    // one tile: [half][128 rows][128 B]
+constexpr int kKVHalf = kN * 128;        // [64 tokens][128 B]
+constexpr int kKVBytes = 4 * kKVHalf;    // K h0, K h1, V h0, V h1
+constexpr int kSoftmaxWarps = 4 * kTiles;
+constexpr int kThreads = (2 + kSoftmaxWarps) * 32;
 constexpr int kBarBytes = 256;
-constexpr int kSmem = 1024 + kQBytes + kStages * kKVBytes + 2 * kPBytes + kBarBytes + 4 * kSmemPages;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColO = 128;
+constexpr int kSmem = 1024 + kTiles * kQBytes + kStages * kKVBytes + kBarBytes + 4 * kSmemPages;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 256;
 }  // namespace tcp
+
+// exp2 on the special-function unit (PTX ex2.approx.ftz.f32, relative error about 2^-22): P is
+// rounded to bf16 (relative step 2^-9) right after, and every argument is <= 8.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __global__ void __launch_bounds__(tcp::kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kvmap,
@@ -406,18 +419,16 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   using namespace tcp;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + kQBytes;
-  uint8_t* sP = sKV + kStages * kKVBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  uint8_t* sQ = smem;  // tile t at t * kQBytes
+  uint8_t* sKV = sQ + kTiles * kQBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kStages * kKVBytes);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;
-  uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
-  uint64_t* o_done = p_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  uint64_t* s_full = kv_empty + kStages;   // [tile][S buffer]
+  uint64_t* p_full = s_full + 2 * kTiles;  // [tile][S buffer]
+  uint64_t* o_done = p_full + 2 * kTiles;  // [tile][S buffer parity of the PV]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2 * kTiles);
   int* info = reinterpret_cast<int*>(tmem_slot + 1);
   int32_t* s_pages = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(bars) + kBarBytes);
 
@@ -426,10 +437,10 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   const int kvh = blockIdx.y;
   const int cta = blockIdx.x;
   const int G = p.group;
-  const int tpt = kM / G;
+  const int tpt = kM / G;  // tokens per tile
   if (threadIdx.x < 32) {
     int seq, tile;
-    longest_first_tile(p.qo_indptr, p.kv_indptr, p.last_len, p.page_size, p.batch, tpt, cta, seq, tile);
+    longest_first_tile(p.qo_indptr, p.kv_indptr, p.last_len, p.page_size, p.batch, kTiles * tpt, cta, seq, tile);
     if (threadIdx.x == 0) {
       info[0] = seq;
       info[1] = tile;
@@ -441,9 +452,8 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 2 * kTiles; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 4);
       mbar_init(&p_full[b], 4);
       mbar_init(&o_done[b], 1);
     }
@@ -459,7 +469,10 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int seq = info[0];
 
-  int nb = 0, q0 = 0, qo_len = 0, n_pages = 0, kv_len = 0, t_first = 0, shift = 0;
+  // blocks each tile needs (0: the tile has no rows); tile B's rows come after tile A's, so nbt[1] is
+  // 0 or >= nbt[0]
+  int nbt[kTiles] = {0, 0};
+  int q0 = 0, qo_len = 0, n_pages = 0, kv_len = 0, t_first = 0, shift = 0;
   if (seq >= 0) {
     q0 = p.qo_indptr[seq];
     qo_len = p.qo_indptr[seq + 1] - q0;
@@ -467,17 +480,22 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
     int ll = p.last_len[seq];
     ll = ll < 1 ? 1 : (ll > p.page_size ? p.page_size : ll);
     kv_len = n_pages > 0 ? (n_pages - 1) * p.page_size + ll : 0;
-    t_first = info[1] * tpt;
-    const int t_last = min(qo_len, t_first + tpt) - 1;
+    t_first = info[1] * kTiles * tpt;
     shift = kv_len - qo_len;
-    const int kv_hi = min(kv_len, shift + t_last + 1);
-    nb = kv_hi > 0 ? (kv_hi + kN - 1) / kN : 0;
+#pragma unroll
+    for (int t = 0; t < kTiles; ++t) {
+      const int f = t_first + t * tpt;
+      const int t_last = min(qo_len, f + tpt) - 1;
+      const int kv_hi = min(kv_len, shift + t_last + 1);
+      nbt[t] = (t_last >= f && kv_hi > 0) ? (kv_hi + kN - 1) / kN : 0;
+    }
   }
+  const int nb = max(nbt[0], nbt[1]);
 
   if (nb > 0) {
     if (warp == 0) {
       // ------------------------------------------------------------ producer
-      // stage the page ids this tile reads in shared memory (one coalesced pass by the warp)
+      // stage the page ids this CTA reads in shared memory (one coalesced pass by the warp)
       const int32_t* pages_g = p.indices + p.kv_indptr[seq];
       const int n_used = min(n_pages, (nb * kN + p.page_size - 1) / p.page_size);
       const bool staged = n_used <= kSmemPages;
@@ -488,9 +506,12 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       if (lane == 0) {
         prefetch_tensormap(&qmap);
         prefetch_tensormap(&kvmap);
-        mbar_arrive_expect_tx(q_full, kQBytes);
-        for (int half = 0; half < 2; ++half)
-          tma_load_3d(sQ + half * (kQBytes / 2), &qmap, q_full, half * 64, kvh * G, q0 + t_first);
+        const int nq = nbt[1] > 0 ? kTiles : 1;
+        mbar_arrive_expect_tx(q_full, nq * kQBytes);
+        for (int t = 0; t < nq; ++t)
+          for (int half = 0; half < 2; ++half)
+            tma_load_3d(sQ + t * kQBytes + half * (kQBytes / 2), &qmap, q_full, half * 64, kvh * G,
+                        q0 + t_first + t * tpt);
       }
       // Lane l issues box l of each block (sub-tile l/4, K or V, dims half): a single thread
       // issuing all 16 boxes serialises on the per-instruction TMA issue cost.
@@ -520,74 +541,89 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       }
     } else if (warp == 1) {
       // ------------------------------------------------------------ MMA issuer
+      // Order per block j: S_A(j), S_B(j), PV_A(j-1), PV_B(j-1).  The tensor pipe runs one thread's MMAs
+      // in issue order, so S_t(j) overwrites S / P buffer (j & 1) of tile t only after PV_t(j-2), issued
+      // before it once P_t(j-2) was complete, has read it.
       if (lane == 0) {
         constexpr uint32_t kIdescS = tc::idesc_bf16_f32(kM, kN, false, false);
         constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(kM, 128, false, true);
         bool ok = mbar_wait(q_full, 0, p.status);
-        auto issue_pv = [&](int i) {
+        auto issue_pv = [&](int t, int i) {
           const int sb = i & 1, s = i % kStages;
-          if (!mbar_wait(&p_full[sb], (i >> 1) & 1, p.status)) {
+          if (!mbar_wait(&p_full[2 * t + sb], (i >> 1) & 1, p.status)) {
             ok = false;
             return;
           }
           tc::fence_after_sync();
-          const uint32_t p_addr = smem_addr(sP + sb * kPBytes);
           const uint32_t v_addr = smem_addr(sKV + s * kKVBytes + 2 * kKVHalf);
 #pragma unroll
           for (int ks = 0; ks < kN / 16; ++ks) {
-            const uint64_t a = tc::smem_desc_sw128(p_addr + ks * 32, 16, 1024);
             const uint64_t b = tc::smem_desc_sw128(v_addr + ks * 2048, kKVHalf, 1024);
-            tc::mma_f16_ss(tmem + kColO, a, b, kIdescPV, (i > 0 || ks > 0) ? 1u : 0u);
+            tc::mma_f16_ts(tmem + kColO + t * 128, tmem + t * 128 + sb * kN + ks * 8, b, kIdescPV,
+                           (i > 0 || ks > 0) ? 1u : 0u);
           }
-          tc::commit(&kv_empty[s]);
-          tc::commit(&o_done[sb]);
+          tc::commit(&o_done[2 * t + sb]);
         };
         const uint32_t q_addr = smem_addr(sQ);
         for (int j = 0; j < nb && ok; ++j) {
           const int s = j % kStages, sb = j & 1;
           if (!mbar_wait(&kv_full[s], (j / kStages) & 1, p.status)) break;
-          if (j >= 2 && !mbar_wait(&s_free[sb], ((j - 2) >> 1) & 1, p.status)) break;
           tc::fence_after_sync();
           const uint32_t k_addr = smem_addr(sKV + s * kKVBytes);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32;
-            const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-            const uint64_t a = tc::smem_desc_sw128(q_addr + off, 16, 1024);
-            const uint64_t b = tc::smem_desc_sw128(k_addr + koff, 16, 1024);
-            tc::mma_f16_ss(tmem + sb * kN, a, b, kIdescS, kk > 0 ? 1u : 0u);
+          for (int t = 0; t < kTiles; ++t) {
+            if (j >= nbt[t]) continue;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint32_t off = t * kQBytes + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32;
+              const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
+              const uint64_t a = tc::smem_desc_sw128(q_addr + off, 16, 1024);
+              const uint64_t b = tc::smem_desc_sw128(k_addr + koff, 16, 1024);
+              tc::mma_f16_ss(tmem + t * 128 + sb * kN, a, b, kIdescS, kk > 0 ? 1u : 0u);
+            }
+            tc::commit(&s_full[2 * t + sb]);
           }
-          tc::commit(&s_full[sb]);
-          if (j >= 1) issue_pv(j - 1);
+          if (j >= 1) {
+#pragma unroll
+            for (int t = 0; t < kTiles; ++t)
+              if (ok && j - 1 < nbt[t]) issue_pv(t, j - 1);
+            // stage (j-1) is free once both tiles' S and PV of block j-1 have completed
+            if (ok) tc::commit(&kv_empty[(j - 1) % kStages]);
+          }
         }
-        if (ok) issue_pv(nb - 1);
+#pragma unroll
+        for (int t = 0; t < kTiles; ++t)
+          if (ok && nb - 1 < nbt[t]) issue_pv(t, nb - 1);
       }
     } else {
       // ------------------------------------------------------------ softmax warps
+      const int t = (warp - 2) >> 2;
+      const int nbx = t == 0 ? nbt[0] : nbt[1];
       const int quarter = warp & 3;
       const int row = quarter * 32 + lane;
       const uint32_t t_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-      const int qtok = t_first + row / G;
+      const uint32_t col_s = t * 128, col_o = kColO + t * 128;
+      uint64_t* sfull = s_full + 2 * t;
+      uint64_t* pfull = p_full + 2 * t;
+      uint64_t* odone = o_done + 2 * t;
+      const int qtok = t_first + t * tpt + row / G;
       const int head = kvh * G + row % G;
       const int lim = shift + qtok;
       const float NEG_INF = -__int_as_float(0x7f800000);
       float m_used = NEG_INF, l = 0.f;
       bool ok = true;
-      for (int j = 0; j < nb && ok; ++j) {
+      for (int j = 0; j < nbx && ok; ++j) {
         const int sb = j & 1;
         const int s = j % kStages;
-        if (!mbar_wait(&s_full[sb], (j >> 1) & 1, p.status)) {
+        if (!mbar_wait(&sfull[sb], (j >> 1) & 1, p.status)) {
           ok = false;
           break;
         }
         tc::fence_after_sync();
         uint32_t sr[64];
-        tc::ld_32x32b_x32(t_row + sb * kN, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        tc::ld_32x32b_x32(t_row + sb * kN + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        tc::ld_32x32b_x32(t_row + col_s + sb * kN, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tc::ld_32x32b_x32(t_row + col_s + sb * kN + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
         tc::wait_ld();
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[sb]);
         const int base = j * kN;
         // raw scores; the causal / length mask only matters on the diagonal and the last block
         if (base + kN - 1 > lim || base + kN > kv_len) {
@@ -613,20 +649,20 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
         const bool need = (m_used != NEG_INF) && (m_new > m_used + 8.f);
         if (__any_sync(kFull, need)) {
           // rescale this warp's O rows once PV(j-1) has landed
-          if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status)) {
+          if (!mbar_wait(&odone[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status)) {
             ok = false;
             break;
           }
           tc::fence_after_sync();
-          const float alpha = need ? exp2f(m_used - m_new) : 1.f;
+          const float alpha = need ? ex2_approx(m_used - m_new) : 1.f;
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) {
             uint32_t o[32];
-            tc::ld_32x32b_x32(t_row + kColO + ch * 32, o);
+            tc::ld_32x32b_x32(t_row + col_o + ch * 32, o);
             tc::wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tc::st_32x32b_x32(t_row + kColO + ch * 32, o);
+            tc::st_32x32b_x32(t_row + col_o + ch * 32, o);
           }
           tc::wait_st();
           if (need) {
@@ -635,44 +671,44 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
           }
         }
         if (m_used == NEG_INF) m_used = m_new;
-        // the P buffer of this parity is free once PV(j-2) has completed
-        if (j >= 2 && !mbar_wait(&o_done[sb], ((j - 2) >> 1) & 1, p.status)) {
-          ok = false;
-          break;
-        }
-        uint8_t* prow = sP + sb * kPBytes + row * 128;
+        // P(j) goes over the first 32 columns of S(j): this thread's row, already in registers
         const float sc = p.scale_log2;
         const float moff = m_used;
         float rs8[8];
+        uint32_t pk[32];
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
           float pv[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) pv[e] = exp2f(fmaf(__uint_as_float(sr[c8 * 8 + e]), sc, -moff));
+          for (int e = 0; e < 8; ++e) pv[e] = ex2_approx(fmaf(__uint_as_float(sr[c8 * 8 + e]), sc, -moff));
           rs8[c8] = ((pv[0] + pv[1]) + (pv[2] + pv[3])) + ((pv[4] + pv[5]) + (pv[6] + pv[7]));
-          *reinterpret_cast<uint4*>(prow + ((c8 ^ (row & 7)) << 4)) =
-              make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]), pack_bf16x2(pv[4], pv[5]),
-                         pack_bf16x2(pv[6], pv[7]));
+          pk[c8 * 4 + 0] = pack_bf16x2(pv[0], pv[1]);
+          pk[c8 * 4 + 1] = pack_bf16x2(pv[2], pv[3]);
+          pk[c8 * 4 + 2] = pack_bf16x2(pv[4], pv[5]);
+          pk[c8 * 4 + 3] = pack_bf16x2(pv[6], pv[7]);
         }
+        tc::st_32x32b_x32(t_row + col_s + sb * kN, pk);
         l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         if (base + kN > kv_len) {
-          // zero V rows at or past kv_len so 0 * stale never meets a NaN
+          // zero V rows at or past kv_len so 0 * stale never meets a NaN (both tiles may write the
+          // same zeros into this block's stage; the stage holds it since kv_full(j))
           const int first_bad = max(0, kv_len - base);
           const int n_bad = kN - first_bad;
           uint8_t* v0 = sKV + s * kKVBytes + 2 * kKVHalf;
-          for (int idx = row; idx < n_bad * 16; idx += 128) {
-            const int t = first_bad + (idx >> 4);
-            const int half = (idx >> 3) & 1, chunk = idx & 7;
-            *reinterpret_cast<uint4*>(v0 + half * kKVHalf + t * 128 + chunk * 16) = make_uint4(0u, 0u, 0u, 0u);
+          for (int idx = row; idx < n_bad * 16; idx += kM) {
+            const int tok = first_bad + (idx >> 4);
+            const int hf = (idx >> 3) & 1, chunk = idx & 7;
+            *reinterpret_cast<uint4*>(v0 + hf * kKVHalf + tok * 128 + chunk * 16) = make_uint4(0u, 0u, 0u, 0u);
           }
+          fence_proxy_async_smem();
         }
-        fence_proxy_async_smem();
+        tc::wait_st();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[sb]);
+        if (lane == 0) mbar_arrive(&pfull[sb]);
       }
-      // epilogue: O / l once the last PV has completed
-      if (ok && mbar_wait(&o_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, p.status)) {
+      // epilogue: O / l once the tile's last PV has completed
+      if (ok && nbx > 0 && mbar_wait(&odone[(nbx - 1) & 1], ((nbx - 1) >> 1) & 1, p.status)) {
         tc::fence_after_sync();
         const float inv = l > 0.f ? 1.f / l : 0.f;
         const bool store = qtok < qo_len;
@@ -681,7 +717,7 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t o[32];
-          tc::ld_32x32b_x32(t_row + kColO + ch * 32, o);
+          tc::ld_32x32b_x32(t_row + col_o + ch * 32, o);
           tc::wait_ld();
           if (store) {
 #pragma unroll
@@ -770,8 +806,8 @@ int launch_prefill_tc(const CUtensorMap& qmap, const CUtensorMap& kvmap, const P
   std::call_once(once, [] {
     cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tcp::kSmem);
   });
-  const int tpt = tcp::kM / a.group;
-  const int grid_x = (total_q + tpt - 1) / tpt + a.batch;
+  const int tokens_per_cta = tcp::kTiles * (tcp::kM / a.group);
+  const int grid_x = (total_q + tokens_per_cta - 1) / tokens_per_cta + a.batch;
   prefill_tc_kernel<<<dim3(grid_x, a.hkv), tcp::kThreads, tcp::kSmem, s>>>(qmap, kvmap, a);
   return check_launch("prefill_attention_tc");
 }

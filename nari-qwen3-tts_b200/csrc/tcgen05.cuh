@@ -1,7 +1,8 @@
 // Fifth-generation tensor core (tcgen05) and Tensor Memory helpers, sm_100a.
 //
 // Inline PTX for: TMEM allocation, single-thread tcgen05.mma (kind::f16,
-// operands from shared memory descriptors, fp32 accumulator in TMEM),
+// B from a shared memory descriptor, A from a descriptor or from TMEM,
+// fp32 accumulator in TMEM),
 // tcgen05.commit to an mbarrier, warp-collective 32x32b TMEM loads/stores
 // and the tcgen05 thread-sync fences; plus the 64-bit shared-memory matrix
 // descriptor and the 32-bit instruction descriptor encodings (PTX ISA,
@@ -46,6 +47,18 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]: A has M rows on the TMEM lanes and its K 16-bit elements
+// packed two per 32-bit column (element 2c in the low half of column c).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
