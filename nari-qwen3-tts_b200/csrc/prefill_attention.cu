@@ -380,8 +380,9 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) prefill_kernel(const __
 // of a one-tile CTA: with one tile, the per-SM delivery of the 16-token K / V boxes (about 20 B per
 // cycle), not the tensor pipe or the softmax, set the time per block.
 //   warp 0       TMA producer (Q of both tiles, then K and V of each block)
-//   warp 1       TMEM allocator and the single MMA-issuing thread
+//   warp 1       TMEM allocator; its lane 0 issues tile A's MMAs
 //   warps 2..5   softmax of tile A, warps 6..9 softmax of tile B: thread = one query row = one TMEM lane
+//   warp 10      lane 0 issues tile B's MMAs
 // TMEM (512 columns): tile t has its S double buffer at [128 t, 128 t + 64) and [128 t + 64, 128 t + 128)
 // and O at [256 + 128 t, 384 + 128 t), all fp32.  S = Q K^T: A = Q (K-major, 128B swizzle), B = K
 // (K-major).  P (bf16, two per column) overwrites the first 32 columns of its own S buffer, and
@@ -398,7 +399,8 @@ constexpr int kQBytes = kM * 128 * 2;    // one tile: [half][128 rows][128 B]
 constexpr int kKVHalf = kN * 128;        // [64 tokens][128 B]
 constexpr int kKVBytes = 4 * kKVHalf;    // K h0, K h1, V h0, V h1
 constexpr int kSoftmaxWarps = 4 * kTiles;
-constexpr int kThreads = (2 + kSoftmaxWarps) * 32;
+constexpr int kIssuerB = 2 + kSoftmaxWarps;  // warp of tile B's MMA-issuing thread
+constexpr int kThreads = (kIssuerB + 1) * 32;
 constexpr int kBarBytes = 256;
 constexpr int kSmem = 1024 + kTiles * kQBytes + kStages * kKVBytes + kBarBytes + 4 * kSmemPages;
 constexpr uint32_t kTmemCols = 512;
@@ -424,8 +426,8 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kStages * kKVBytes);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;   // [tile][S buffer]
+  uint64_t* kv_empty = kv_full + kStages;  // [tile][stage]: the tile's S and PV of the stage's block are done
+  uint64_t* s_full = kv_empty + kTiles * kStages;  // [tile][S buffer]
   uint64_t* p_full = s_full + 2 * kTiles;  // [tile][S buffer]
   uint64_t* o_done = p_full + 2 * kTiles;  // [tile][S buffer parity of the PV]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2 * kTiles);
@@ -448,10 +450,8 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
   }
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-    }
+    for (int s = 0; s < kStages; ++s) mbar_init(&kv_full[s], 1);
+    for (int s = 0; s < kTiles * kStages; ++s) mbar_init(&kv_empty[s], 1);
     for (int b = 0; b < 2 * kTiles; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 4);
@@ -518,8 +518,15 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
       const int sub = lane >> 2, kind = (lane >> 1) & 1, half = lane & 1;
       for (int j = 0; j < nb; ++j) {
         const int s = j % kStages;
-        // warp-uniform decision: every lane reaches the same __syncwarp
-        const bool ready = j < kStages || mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, p.status);
+        // warp-uniform decision: every lane reaches the same __syncwarp.  The stage's previous block,
+        // j - kStages, is released by each tile that read it
+        bool ready = true;
+        if (j >= kStages) {
+#pragma unroll
+          for (int t = 0; t < kTiles; ++t)
+            if (j - kStages < nbt[t] && !mbar_wait(&kv_empty[t * kStages + s], ((j / kStages) - 1) & 1, p.status))
+              ready = false;
+        }
         if (!__all_sync(kFull, ready)) break;
         if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], kKVBytes);
         __syncwarp();
@@ -539,64 +546,63 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
                       kvh, tip, page * 2 + kind);
         }
       }
-    } else if (warp == 1) {
-      // ------------------------------------------------------------ MMA issuer
-      // Order per block j: S_A(j), S_B(j), PV_A(j-1), PV_B(j-1).  The tensor pipe runs one thread's MMAs
-      // in issue order, so S_t(j) overwrites S / P buffer (j & 1) of tile t only after PV_t(j-2), issued
-      // before it once P_t(j-2) was complete, has read it.
-      if (lane == 0) {
+    } else if (warp == 1 || warp == kIssuerB) {
+      // ------------------------------------------------------------ MMA issuers
+      // One thread per tile (warp 1: tile A, warp kIssuerB: tile B), so neither tile's MMAs queue
+      // behind the other's waits.  Order per tile: S(0), S(1), then per block j: PV(j), S(j+2).
+      // S(j+2) reuses the tile's S / P buffer (j & 1); the tensor pipe runs one thread's MMAs in issue
+      // order, so it overwrites P(j) only after PV(j) has read it.
+      const int t = warp == 1 ? 0 : 1;
+      const int nbx = t == 0 ? nbt[0] : nbt[1];
+      if (lane == 0 && nbx > 0) {
         constexpr uint32_t kIdescS = tc::idesc_bf16_f32(kM, kN, false, false);
         constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(kM, 128, false, true);
         bool ok = mbar_wait(q_full, 0, p.status);
-        auto issue_pv = [&](int t, int i) {
+        // descriptors are built once; a byte offset inside shared memory (< 256 KB) moves only the
+        // 14-bit start-address field, so it is added to the descriptor as offset >> 4
+        const uint64_t q_desc = tc::smem_desc_sw128(smem_addr(sQ + t * kQBytes), 16, 1024);
+        const uint64_t k_desc = tc::smem_desc_sw128(smem_addr(sKV), 16, 1024);
+        const uint64_t v_desc = tc::smem_desc_sw128(smem_addr(sKV + 2 * kKVHalf), kKVHalf, 1024);
+        const uint32_t s_cols = tmem + t * 128, o_cols = tmem + kColO + t * 128;
+        auto issue_s = [&](int j) {
+          if (!mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, p.status)) {
+            ok = false;
+            return;
+          }
+          tc::fence_after_sync();
+          const int sb = j & 1;
+          const uint64_t kd = k_desc + static_cast<uint32_t>(((j % kStages) * kKVBytes) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = ((kk >> 2) * (kQBytes / 2) + (kk & 3) * 32) >> 4;
+            const uint32_t koff = ((kk >> 2) * kKVHalf + (kk & 3) * 32) >> 4;
+            tc::mma_f16_ss(s_cols + sb * kN, q_desc + off, kd + koff, kIdescS, kk > 0 ? 1u : 0u);
+          }
+          tc::commit(&s_full[2 * t + sb]);
+        };
+        auto issue_pv = [&](int i) {
           const int sb = i & 1, s = i % kStages;
           if (!mbar_wait(&p_full[2 * t + sb], (i >> 1) & 1, p.status)) {
             ok = false;
             return;
           }
           tc::fence_after_sync();
-          const uint32_t v_addr = smem_addr(sKV + s * kKVBytes + 2 * kKVHalf);
+          const uint64_t vd = v_desc + static_cast<uint32_t>((s * kKVBytes) >> 4);
 #pragma unroll
-          for (int ks = 0; ks < kN / 16; ++ks) {
-            const uint64_t b = tc::smem_desc_sw128(v_addr + ks * 2048, kKVHalf, 1024);
-            tc::mma_f16_ts(tmem + kColO + t * 128, tmem + t * 128 + sb * kN + ks * 8, b, kIdescPV,
+          for (int ks = 0; ks < kN / 16; ++ks)
+            tc::mma_f16_ts(o_cols, s_cols + sb * kN + ks * 8, vd + ((ks * 2048) >> 4), kIdescPV,
                            (i > 0 || ks > 0) ? 1u : 0u);
-          }
           tc::commit(&o_done[2 * t + sb]);
+          tc::commit(&kv_empty[t * kStages + s]);  // this tile's S(i) and PV(i) have read stage s
         };
-        const uint32_t q_addr = smem_addr(sQ);
-        for (int j = 0; j < nb && ok; ++j) {
-          const int s = j % kStages, sb = j & 1;
-          if (!mbar_wait(&kv_full[s], (j / kStages) & 1, p.status)) break;
-          tc::fence_after_sync();
-          const uint32_t k_addr = smem_addr(sKV + s * kKVBytes);
-#pragma unroll
-          for (int t = 0; t < kTiles; ++t) {
-            if (j >= nbt[t]) continue;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint32_t off = t * kQBytes + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32;
-              const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-              const uint64_t a = tc::smem_desc_sw128(q_addr + off, 16, 1024);
-              const uint64_t b = tc::smem_desc_sw128(k_addr + koff, 16, 1024);
-              tc::mma_f16_ss(tmem + t * 128 + sb * kN, a, b, kIdescS, kk > 0 ? 1u : 0u);
-            }
-            tc::commit(&s_full[2 * t + sb]);
-          }
-          if (j >= 1) {
-#pragma unroll
-            for (int t = 0; t < kTiles; ++t)
-              if (ok && j - 1 < nbt[t]) issue_pv(t, j - 1);
-            // stage (j-1) is free once both tiles' S and PV of block j-1 have completed
-            if (ok) tc::commit(&kv_empty[(j - 1) % kStages]);
-          }
+        for (int j = 0; j < 2 && j < nbx && ok; ++j) issue_s(j);
+        for (int j = 0; j < nbx && ok; ++j) {
+          issue_pv(j);
+          if (ok && j + 2 < nbx) issue_s(j + 2);
         }
-#pragma unroll
-        for (int t = 0; t < kTiles; ++t)
-          if (ok && nb - 1 < nbt[t]) issue_pv(t, nb - 1);
       }
     } else {
-      // ------------------------------------------------------------ softmax warps
+      // ------------------------------------------------------------ softmax warps (2 .. kIssuerB - 1)
       const int t = (warp - 2) >> 2;
       const int nbx = t == 0 ? nbt[0] : nbt[1];
       const int quarter = warp & 3;
