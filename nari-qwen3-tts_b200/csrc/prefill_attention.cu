@@ -415,6 +415,33 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Three-input max and packed two-lane fp32 arithmetic (sm_100 FMNMX3 / FFMA2 / FADD2): half the
+// instructions of the scalar forms for the softmax's row max, scale-and-shift and row sum.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2(float lo, float hi) { return f2(__float_as_uint(lo), __float_as_uint(hi)); }
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __global__ void __launch_bounds__(tcp::kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kvmap,
                       PrefillArgs p) {
@@ -642,14 +669,12 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
         float mx8[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          float a = fmaxf(fmaxf(__uint_as_float(sr[e]), __uint_as_float(sr[e + 8])),
-                          fmaxf(__uint_as_float(sr[e + 16]), __uint_as_float(sr[e + 24])));
-          float b = fmaxf(fmaxf(__uint_as_float(sr[e + 32]), __uint_as_float(sr[e + 40])),
-                          fmaxf(__uint_as_float(sr[e + 48]), __uint_as_float(sr[e + 56])));
-          mx8[e] = fmaxf(a, b);
+          const float a = max3f(__uint_as_float(sr[e]), __uint_as_float(sr[e + 8]), __uint_as_float(sr[e + 16]));
+          const float b = max3f(a, __uint_as_float(sr[e + 24]), __uint_as_float(sr[e + 32]));
+          const float c = max3f(b, __uint_as_float(sr[e + 40]), __uint_as_float(sr[e + 48]));
+          mx8[e] = fmaxf(c, __uint_as_float(sr[e + 56]));
         }
-        const float mx_raw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float mx_raw = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
         const float mx = mx_raw * p.scale_log2;  // log2 domain (scale > 0 keeps the order)
         const float m_new = fmaxf(m_used, mx);
         const bool need = (m_used != NEG_INF) && (m_new > m_used + 8.f);
@@ -678,23 +703,32 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
         }
         if (m_used == NEG_INF) m_used = m_new;
         // P(j) goes over the first 32 columns of S(j): this thread's row, already in registers
-        const float sc = p.scale_log2;
-        const float moff = m_used;
-        float rs8[8];
+        const uint64_t sc2 = f2(p.scale_log2, p.scale_log2);
+        const uint64_t mo2 = f2(-m_used, -m_used);
+        uint64_t rs2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};  // row-sum partials, two lanes each
         uint32_t pk[32];
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
+          uint64_t x2[4];
           float pv[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) pv[e] = ex2_approx(fmaf(__uint_as_float(sr[c8 * 8 + e]), sc, -moff));
-          rs8[c8] = ((pv[0] + pv[1]) + (pv[2] + pv[3])) + ((pv[4] + pv[5]) + (pv[6] + pv[7]));
-          pk[c8 * 4 + 0] = pack_bf16x2(pv[0], pv[1]);
-          pk[c8 * 4 + 1] = pack_bf16x2(pv[2], pv[3]);
-          pk[c8 * 4 + 2] = pack_bf16x2(pv[4], pv[5]);
-          pk[c8 * 4 + 3] = pack_bf16x2(pv[6], pv[7]);
+          for (int q = 0; q < 4; ++q) {
+            x2[q] = f2_fma(f2(sr[c8 * 8 + 2 * q], sr[c8 * 8 + 2 * q + 1]), sc2, mo2);
+            float lo, hi;
+            f2_split(x2[q], lo, hi);
+            pv[2 * q] = ex2_approx(lo);
+            pv[2 * q + 1] = ex2_approx(hi);
+            pk[c8 * 4 + q] = pack_bf16x2(pv[2 * q], pv[2 * q + 1]);
+          }
+          const uint64_t r = f2_add(f2_add(f2(pv[0], pv[1]), f2(pv[2], pv[3])), f2_add(f2(pv[4], pv[5]), f2(pv[6], pv[7])));
+          rs2[c8 & 1] = f2_add(rs2[c8 & 1], r);
         }
         tc::st_32x32b_x32(t_row + col_s + sb * kN, pk);
-        l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+        {
+          float lo, hi;
+          f2_split(f2_add(rs2[0], rs2[1]), lo, hi);
+          l += lo + hi;
+        }
         if (base + kN > kv_len) {
           // zero V rows at or past kv_len so 0 * stale never meets a NaN (both tiles may write the
           // same zeros into this block's stage; the stage holds it since kv_full(j))
