@@ -129,8 +129,11 @@ __global__ void __launch_bounds__((kConsumers + 1) * 32) prefill_kernel(const __
   uint64_t* empty = full + STAGES;
   int* s_info = reinterpret_cast<int*>(empty + STAGES);
 
-  const int kvh = blockIdx.y;
-  const int cta = blockIdx.x;
+  // 1-D grid, KV head fastest: CTAs start in blockIdx order, so the heaviest tiles of every head go
+  // out in the first wave (a (tiles, heads) grid would start all of head 0's tiles, light ones
+  // included, before head 1's heaviest)
+  const int kvh = blockIdx.x % p.hkv;
+  const int cta = blockIdx.x / p.hkv;
   const int G = p.group;
   const int tokens_per_tile = kRows / G;
   if (threadIdx.x < 32) {
@@ -463,8 +466,11 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int kvh = blockIdx.y;
-  const int cta = blockIdx.x;
+  // 1-D grid, KV head fastest: CTAs start in blockIdx order, so the heaviest tiles of every head go
+  // out in the first wave (a (tiles, heads) grid would start all of head 0's tiles, light ones
+  // included, before head 1's heaviest)
+  const int kvh = blockIdx.x % p.hkv;
+  const int cta = blockIdx.x / p.hkv;
   const int G = p.group;
   const int tpt = kM / G;  // tokens per tile
   if (threadIdx.x < 32) {
@@ -848,7 +854,7 @@ int launch_prefill_tc(const CUtensorMap& qmap, const CUtensorMap& kvmap, const P
   });
   const int tokens_per_cta = tcp::kTiles * (tcp::kM / a.group);
   const int grid_x = (total_q + tokens_per_cta - 1) / tokens_per_cta + a.batch;
-  prefill_tc_kernel<<<dim3(grid_x, a.hkv), tcp::kThreads, tcp::kSmem, s>>>(qmap, kvmap, a);
+  prefill_tc_kernel<<<dim3(grid_x * a.hkv), tcp::kThreads, tcp::kSmem, s>>>(qmap, kvmap, a);
   return check_launch("prefill_attention_tc");
 }
 
@@ -859,7 +865,7 @@ int launch_prefill(const CUtensorMap& map, const PrefillArgs& a, int grid_x, cud
   std::call_once(once, [] {
     cudaFuncSetAttribute(prefill_kernel<D, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
   });
-  prefill_kernel<D, STAGES><<<dim3(grid_x, a.hkv), Cfg::kThreads, Cfg::kSmem, s>>>(map, a);
+  prefill_kernel<D, STAGES><<<dim3(grid_x * a.hkv), Cfg::kThreads, Cfg::kSmem, s>>>(map, a);
   return check_launch("prefill_attention");
 }
 

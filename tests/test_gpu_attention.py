@@ -117,6 +117,17 @@ def test_prefill_matches_oracle(nqt, cuda, lens, qo_lens):
     torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
 
 
+def test_prefill_ragged_query_tile_pairs(nqt, cuda):
+    # a CTA computes two query tiles of 128 / G tokens: chunks that end inside the first tile, exactly
+    # at its end, inside and at the end of the second, over short and long contexts, one key block of
+    # context or none
+    lens = [129, 1, 94, 65, 227, 128, 256, 257, 1033, 64, 191]
+    qo_lens = [129, 1, 30, 65, 100, 128, 1, 257, 333, 64, 127]
+    got, want = _prefill_case(nqt, cuda, lens, qo_lens, seed=9)
+    assert torch.isfinite(got).all()
+    torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
+
+
 @pytest.mark.parametrize(("hq", "hkv", "d", "page_size"), [(16, 8, 64, 16), (8, 8, 128, 32), (16, 2, 128, 64)])
 def test_prefill_layouts(nqt, cuda, hq, hkv, d, page_size):
     got, want = _prefill_case(nqt, cuda, [90, 260], [90, 31], hq=hq, hkv=hkv, d=d, page_size=page_size, seed=7)
