@@ -42,6 +42,7 @@ struct PrefillArgs {
   int32_t* status;
   int batch, hq, hkv, group, page_size, total_pages;
   float scale_log2;
+  int tma_out;  // tcgen05 path: full query tiles leave through a TMA store (out map valid)
 };
 
 template <int D, int STAGES>
@@ -445,9 +446,23 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   return d;
 }
 
+// TMA store of a 3-D box from shared memory (bulk group), its commit and the wait until the
+// shared-memory source has been read; a named barrier over `n` threads.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_addr(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 __global__ void __launch_bounds__(tcp::kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kvmap,
-                      PrefillArgs p) {
+                      const __grid_constant__ CUtensorMap omap, PrefillArgs p) {
   using namespace tcp;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -753,29 +768,50 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&pfull[sb]);
       }
-      // epilogue: O / l once the tile's last PV has completed
-      if (ok && nbx > 0 && mbar_wait(&odone[(nbx - 1) & 1], ((nbx - 1) >> 1) & 1, p.status)) {
+      // epilogue: O / l once the tile's last PV has completed.  A full tile (every row inside the
+      // chunk) is written as bf16 into its own Q buffer (free: its last reader, S(nbx - 1), completed
+      // before the last PV) in the Q box layout and leaves through one TMA store per 64 dims; a
+      // ragged tile is stored row by row.  Every thread of the tile reaches the named barrier.
+      const bool full = p.tma_out && nbx > 0 && t_first + (t + 1) * tpt <= qo_len;
+      const bool have = ok && nbx > 0 && mbar_wait(&odone[(nbx - 1) & 1], ((nbx - 1) >> 1) & 1, p.status);
+      if (have) {
         tc::fence_after_sync();
         const float inv = l > 0.f ? 1.f / l : 0.f;
         const bool store = qtok < qo_len;
         __nv_bfloat16* orow =
             p.out + static_cast<int64_t>(q0 + qtok) * p.o_st + static_cast<int64_t>(head) * p.o_sh;
+        uint8_t* srow = sQ + t * kQBytes + row * 128;
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t o[32];
           tc::ld_32x32b_x32(t_row + col_o + ch * 32, o);
           tc::wait_ld();
-          if (store) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 pk;
-              pk.x = pack_bf16x2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
-              pk.y = pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
-              pk.z = pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
-              pk.w = pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+          for (int v = 0; v < 4; ++v) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
+            pk.y = pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
+            pk.z = pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
+            pk.w = pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+            if (full) {
+              // dims 32 ch + 8 v: half ch / 2, 16-byte chunk (ch % 2) * 4 + v, 128B-swizzled by row
+              const int chunk = (ch & 1) * 4 + v;
+              *reinterpret_cast<uint4*>(srow + (ch >> 1) * (kQBytes / 2) + ((chunk ^ (row & 7)) << 4)) = pk;
+            } else if (store) {
               *reinterpret_cast<uint4*>(orow + ch * 32 + v * 8) = pk;
             }
           }
+        }
+      }
+      if (full) {
+        fence_proxy_async_smem();
+        named_bar_sync(1 + t, 4 * 32);
+        if (quarter == 2 && lane == 0) {  // warp 2 + 4 t
+          for (int half = 0; half < 2; ++half)
+            tma_store_3d(&omap, sQ + t * kQBytes + half * (kQBytes / 2), half * 64, kvh * G,
+                         q0 + t_first + t * tpt);
+          bulk_commit_group();
+          bulk_wait_group_read0();  // the Q buffer stays valid until the store has read it
         }
       }
     }
@@ -846,15 +882,15 @@ int encode_q_map(CUtensorMap* map, const void* q, int64_t q_st, int64_t q_sh, in
   return r == CUDA_SUCCESS ? NQT_OK : NQT_ERR_CUDA;
 }
 
-int launch_prefill_tc(const CUtensorMap& qmap, const CUtensorMap& kvmap, const PrefillArgs& a, int total_q,
-                      cudaStream_t s) {
+int launch_prefill_tc(const CUtensorMap& qmap, const CUtensorMap& kvmap, const CUtensorMap& omap,
+                      const PrefillArgs& a, int total_q, cudaStream_t s) {
   static std::once_flag once;
   std::call_once(once, [] {
     cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tcp::kSmem);
   });
   const int tokens_per_cta = tcp::kTiles * (tcp::kM / a.group);
   const int grid_x = (total_q + tokens_per_cta - 1) / tokens_per_cta + a.batch;
-  prefill_tc_kernel<<<dim3(grid_x * a.hkv), tcp::kThreads, tcp::kSmem, s>>>(qmap, kvmap, a);
+  prefill_tc_kernel<<<dim3(grid_x * a.hkv), tcp::kThreads, tcp::kSmem, s>>>(qmap, kvmap, omap, a);
   return check_launch("prefill_attention_tc");
 }
 
@@ -922,8 +958,14 @@ extern "C" int nqt_prefill_attention(const void* q, int64_t q_stride_tok, int64_
     if (rc != NQT_OK) return rc;
     rc = encode_kv_map_single(&kvmap, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
     if (rc != NQT_OK) return rc;
-    return launch_prefill_tc(qmap, kvmap, a, total_q_tokens, s);
+    // full query tiles leave through a TMA store when out allows a tensor map (16-byte aligned base
+    // and strides); otherwise every row is stored by its thread
+    CUtensorMap omap{};
+    a.tma_out = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && out_stride_tok % 8 == 0 && out_stride_head % 8 == 0 &&
+                encode_q_map(&omap, out, out_stride_tok, out_stride_head, total_q_tokens, num_qo_heads, group) == NQT_OK;
+    return launch_prefill_tc(qmap, kvmap, omap, a, total_q_tokens, s);
   }
+  a.tma_out = 0;
   CUtensorMap map;
   int rc = encode_map(&map, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
   if (rc != NQT_OK) return rc;
