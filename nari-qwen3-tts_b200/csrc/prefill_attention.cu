@@ -768,19 +768,18 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&pfull[sb]);
       }
-      // epilogue: O / l once the tile's last PV has completed.  A full tile (every row inside the
-      // chunk) is written as bf16 into its own Q buffer (free: its last reader, S(nbx - 1), completed
-      // before the last PV) in the Q box layout and leaves through one TMA store per 64 dims; a
-      // ragged tile is stored row by row.  Every thread of the tile reaches the named barrier.
-      const bool full = p.tma_out && nbx > 0 && t_first + (t + 1) * tpt <= qo_len;
+      // epilogue: O / l once the tile's last PV has completed, written as bf16 into the tile's own Q
+      // buffer (free: its last reader, S(nbx - 1), completed before the last PV) in the Q box layout.
+      // A full tile (every row inside the chunk) leaves through one TMA store per 64 dims; a ragged
+      // one through coalesced 16-byte stores of its valid rows (a warp covers two whole rows).  Every
+      // thread of the tile reaches the named barrier.
+      const bool full = p.tma_out && t_first + (t + 1) * tpt <= qo_len;
       const bool have = ok && nbx > 0 && mbar_wait(&odone[(nbx - 1) & 1], ((nbx - 1) >> 1) & 1, p.status);
+      uint8_t* sO = sQ + t * kQBytes;
       if (have) {
         tc::fence_after_sync();
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        const bool store = qtok < qo_len;
-        __nv_bfloat16* orow =
-            p.out + static_cast<int64_t>(q0 + qtok) * p.o_st + static_cast<int64_t>(head) * p.o_sh;
-        uint8_t* srow = sQ + t * kQBytes + row * 128;
+        uint8_t* srow = sO + row * 128;
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t o[32];
@@ -793,25 +792,34 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
             pk.y = pack_bf16x2(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
             pk.z = pack_bf16x2(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
             pk.w = pack_bf16x2(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
-            if (full) {
-              // dims 32 ch + 8 v: half ch / 2, 16-byte chunk (ch % 2) * 4 + v, 128B-swizzled by row
-              const int chunk = (ch & 1) * 4 + v;
-              *reinterpret_cast<uint4*>(srow + (ch >> 1) * (kQBytes / 2) + ((chunk ^ (row & 7)) << 4)) = pk;
-            } else if (store) {
-              *reinterpret_cast<uint4*>(orow + ch * 32 + v * 8) = pk;
-            }
+            // dims 32 ch + 8 v: half ch / 2, 16-byte chunk (ch % 2) * 4 + v, 128B-swizzled by row
+            const int chunk = (ch & 1) * 4 + v;
+            *reinterpret_cast<uint4*>(srow + (ch >> 1) * (kQBytes / 2) + ((chunk ^ (row & 7)) << 4)) = pk;
           }
         }
       }
-      if (full) {
-        fence_proxy_async_smem();
+      if (nbx > 0) {
+        if (full) fence_proxy_async_smem();
         named_bar_sync(1 + t, 4 * 32);
-        if (quarter == 2 && lane == 0) {  // warp 2 + 4 t
-          for (int half = 0; half < 2; ++half)
-            tma_store_3d(&omap, sQ + t * kQBytes + half * (kQBytes / 2), half * 64, kvh * G,
-                         q0 + t_first + t * tpt);
-          bulk_commit_group();
-          bulk_wait_group_read0();  // the Q buffer stays valid until the store has read it
+        if (full) {
+          if (quarter == 2 && lane == 0) {  // warp 2 + 4 t
+            for (int half = 0; half < 2; ++half)
+              tma_store_3d(&omap, sO + half * (kQBytes / 2), half * 64, kvh * G, q0 + t_first + t * tpt);
+            bulk_commit_group();
+            bulk_wait_group_read0();  // the Q buffer stays valid until the store has read it
+          }
+        } else {
+          // 128 rows x 16 chunks of 16 bytes; consecutive threads take consecutive chunks of a row
+          for (int i = row; i < kM * 16; i += kM) {
+            const int r = i >> 4, c = i & 15;
+            const int tok = t_first + t * tpt + r / G;
+            if (tok < qo_len) {
+              const uint4 v = *reinterpret_cast<const uint4*>(sO + (c >> 3) * (kQBytes / 2) + r * 128 +
+                                                              (((c & 7) ^ (r & 7)) << 4));
+              *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(q0 + tok) * p.o_st +
+                                        static_cast<int64_t>(kvh * G + r % G) * p.o_sh + c * 8) = v;
+            }
+          }
         }
       }
     }
