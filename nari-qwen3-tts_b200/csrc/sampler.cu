@@ -832,9 +832,11 @@ __host__ __device__ constexpr size_t region_bytes(int vocab, size_t group_bytes)
   return static_cast<size_t>(vocab) * 4 > group_bytes ? static_cast<size_t>(vocab) * 4 : group_bytes;
 }
 
-// kWarps / G rows per CTA, G warps per row.
+// kWarps / G rows per CTA, G warps per row.  Four CTAs per SM (at most 64 registers per thread, no
+// spills; about 45 KB of shared memory each): the passes are bound by instruction latency, so more
+// resident warps help (16384 x 3072 rows: 234 -> 179 us against two CTAs per SM).
 template <typename T, int G>
-__global__ void __launch_bounds__(kThreads, 2) sample_kernel(SampleArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) sample_kernel(SampleArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ BlockShared bs;
   __shared__ int s_rest[kWarps];
