@@ -43,6 +43,7 @@ struct PrefillArgs {
   int batch, hq, hkv, group, page_size, total_pages;
   float scale_log2;
   int tma_out;  // tcgen05 path: full query tiles leave through a TMA store (out map valid)
+  int out16;    // tcgen05 path: every output row chunk is 16-byte aligned (else 4-byte stores)
 };
 
 template <int D, int STAGES>
@@ -816,8 +817,17 @@ __global__ void __launch_bounds__(tcp::kThreads, 1)
             if (tok < qo_len) {
               const uint4 v = *reinterpret_cast<const uint4*>(sO + (c >> 3) * (kQBytes / 2) + r * 128 +
                                                               (((c & 7) ^ (r & 7)) << 4));
-              *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(q0 + tok) * p.o_st +
-                                        static_cast<int64_t>(kvh * G + r % G) * p.o_sh + c * 8) = v;
+              __nv_bfloat16* dst =
+                  p.out + static_cast<int64_t>(q0 + tok) * p.o_st + static_cast<int64_t>(kvh * G + r % G) * p.o_sh + c * 8;
+              if (p.out16) {
+                *reinterpret_cast<uint4*>(dst) = v;
+              } else {  // out and its strides are only 4-byte aligned
+                uint32_t* d4 = reinterpret_cast<uint32_t*>(dst);
+                d4[0] = v.x;
+                d4[1] = v.y;
+                d4[2] = v.z;
+                d4[3] = v.w;
+              }
             }
           }
         }
@@ -969,11 +979,13 @@ extern "C" int nqt_prefill_attention(const void* q, int64_t q_stride_tok, int64_
     // full query tiles leave through a TMA store when out allows a tensor map (16-byte aligned base
     // and strides); otherwise every row is stored by its thread
     CUtensorMap omap{};
-    a.tma_out = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && out_stride_tok % 8 == 0 && out_stride_head % 8 == 0 &&
+    a.out16 = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && out_stride_tok % 8 == 0 && out_stride_head % 8 == 0;
+    a.tma_out = a.out16 &&
                 encode_q_map(&omap, out, out_stride_tok, out_stride_head, total_q_tokens, num_qo_heads, group) == NQT_OK;
     return launch_prefill_tc(qmap, kvmap, omap, a, total_q_tokens, s);
   }
   a.tma_out = 0;
+  a.out16 = 0;
   CUtensorMap map;
   int rc = encode_map(&map, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
   if (rc != NQT_OK) return rc;

@@ -128,6 +128,26 @@ def test_prefill_ragged_query_tile_pairs(nqt, cuda):
     torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
 
 
+def test_prefill_output_without_a_tensor_map_layout(nqt, cuda):
+    # full query tiles normally leave through a TMA store; an output whose token stride is not a
+    # multiple of 16 bytes cannot take a tensor map, so every tile goes through the row stores.
+    # Both layouts must hold the same values, and the padding columns stay untouched
+    lens, qo_lens = [300, 257, 128], [256, 257, 128]
+    cache, indptr, indices, last = make_paged(lens, seed=11)
+    qo_indptr = torch.tensor([0, *torch.tensor(qo_lens).cumsum(0).tolist()], dtype=torch.int32)
+    tokens = int(qo_indptr[-1])
+    q = torch.randn(tokens, 16, 128, generator=torch.Generator().manual_seed(12)).to(torch.bfloat16).to(cuda)
+    args = (cache.to(cuda), qo_indptr.to(cuda), indptr.to(cuda), indices.to(cuda), last.to(cuda))
+    dense = nqt.batch_prefill_paged(q, *args)
+    padded = torch.full((tokens, 16 * 128 + 4), 7.0, dtype=torch.bfloat16, device=cuda)
+    view = padded[:, : 16 * 128].view(tokens, 16, 128)
+    assert view.stride(0) % 8 != 0
+    nqt.batch_prefill_paged(q, *args, out=view)
+    torch.cuda.synchronize()
+    assert torch.equal(view, dense)
+    assert bool((padded[:, 16 * 128:] == 7.0).all())
+
+
 @pytest.mark.parametrize(("hq", "hkv", "d", "page_size"), [(16, 8, 64, 16), (8, 8, 128, 32), (16, 2, 128, 64)])
 def test_prefill_layouts(nqt, cuda, hq, hkv, d, page_size):
     got, want = _prefill_case(nqt, cuda, [90, 260], [90, 31], hq=hq, hkv=hkv, d=d, page_size=page_size, seed=7)
