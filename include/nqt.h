@@ -202,6 +202,10 @@ size_t nqt_decode_noalloc_scratch_bytes(void);
  * positions of that sequence's KV, so query i sees KV positions
  * <= kv_len - qo_len + i.  Replaces BatchPrefillWithPagedKVCacheWrapper.run
  * (executor/talker_kv.py:225-226, causal=True).
+ * out needs 4-byte alignment and even strides.  With head_dim 128, a 16-byte
+ * aligned out whose strides are multiples of 8 elements lets every full
+ * 128-row query tile leave through one TMA store (the fast path); any other
+ * accepted layout is written with 4-byte stores.
  */
 int nqt_prefill_attention(
     const void* q, int64_t q_stride_tok, int64_t q_stride_head,
