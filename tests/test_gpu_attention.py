@@ -128,6 +128,22 @@ def test_prefill_ragged_query_tile_pairs(nqt, cuda):
     torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
 
 
+@pytest.mark.parametrize("seed", range(6))
+def test_prefill_random_batches(nqt, cuda, seed):
+    # seeded random batches: 1-9 sequences, chunks of 1-400 tokens over 0-600 tokens of context, the
+    # four GQA groups the kernel takes (128 / G tokens per query tile) and three page sizes
+    g = torch.Generator().manual_seed(1000 + seed)
+    hq, hkv = [(8, 8), (16, 8), (16, 4), (16, 2)][seed % 4]
+    page_size = [16, 32, 64][seed % 3]
+    b = int(torch.randint(1, 10, (1,), generator=g))
+    qo_lens = torch.randint(1, 401, (b,), generator=g).tolist()
+    ctx = torch.randint(0, 601, (b,), generator=g).tolist()
+    lens = [q + c for q, c in zip(qo_lens, ctx)]
+    got, want = _prefill_case(nqt, cuda, lens, qo_lens, page_size=page_size, hq=hq, hkv=hkv, seed=seed)
+    assert torch.isfinite(got).all()
+    torch.testing.assert_close(got, want, atol=ATOL, rtol=0)
+
+
 def test_prefill_output_without_a_tensor_map_layout(nqt, cuda):
     # full query tiles normally leave through a TMA store; an output whose token stride is not a
     # multiple of 16 bytes cannot take a tensor map, so every tile goes through the row stores.
