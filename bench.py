@@ -16,10 +16,14 @@ Reported on the JSON line besides the throughput:
   roofline     the decode-attention launch (one decode kernel, fused fix-up) timed
                alone with CUDA events over the same metadata: algorithmic
                KV + q + out bytes / duration vs the measured HBM copy peak;
-  cpu_baseline the CPU port of the step (oracle/talker_step.py) on a bounded
-               sample (rank 0, N = 1);
+  sampler_roofline  the fused sampler on 256 stacked talker steps (16384 x
+               3072 rows) timed in the same process: algorithmic logits +
+               seen-mask bytes / duration vs the measured HBM copy peak;
+  cpu_baseline whole steps of the CPU port (oracle/talker_step.py: every
+               layer, every row) for about --cpu-seconds (rank 0, N = 1);
   clocks       nvidia-smi samples taken during the timed region.
-``--impl reference`` times the CPU port alone (the reference arm).
+``--impl reference`` times whole steps of the CPU port alone (the reference
+arm), on rank 0 only at every N.
 """
 
 from __future__ import annotations
@@ -56,7 +60,7 @@ def parse() -> argparse.Namespace:
                    help="decode = BASELINE config 2 (the headline); mixed = config 4 (prefill chunks + decode rows)")
     p.add_argument("--layers", type=int, default=28, help="decoder layers (28 = BASELINE config 2)")
     p.add_argument("--pool-tokens", type=int, default=POOL_TOKENS)
-    p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
+    p.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--grow", action="store_true",
                    help="publish each step (contexts grow by one token per step) instead of holding them fixed")
@@ -161,54 +165,65 @@ def max_over_ranks(value: float, world: int) -> float:
     return float(t.item())
 
 
-def cpu_baseline(budget_s: float, layers: int) -> dict:
+def _cpu_port(layers: int):
     from oracle.talker_step import CpuTalkerStep
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     step = CpuTalkerStep(contexts=contexts_for(0), num_layers=layers)
-    step.time_step(layers=1)  # warm-up
+    step.time_step(layers=2)  # warm-up: first-touch of the weights, caches and the allocator
+    return step, threads
+
+
+def cpu_baseline(budget_s: float, layers: int) -> dict:
+    """Whole steps of the CPU port (every row, every layer) until ``budget_s`` is spent (at least one)."""
+
+    step, threads = _cpu_port(layers)
     runs = []
     t_end = time.perf_counter() + budget_s
     while time.perf_counter() < t_end or not runs:
-        runs.append(step.time_step(layers=1))
-    full = statistics.mean(r["full_step_s"] for r in runs)
+        runs.append(step.time_step()["step_s"])
+    per_step = statistics.mean(runs)
     return {
-        "value": BATCH / full,
+        "value": BATCH / per_step,
         "unit": UNIT,
         "cores": threads,
         "kind": "port",
-        "sample": (f"{len(runs)} sampled steps of the CPU port (oracle/talker_step.py): host planner for all "
-                   f"{BATCH} rows, 1 of {layers} decoder layers and the head + sampler for all rows in fp32, "
-                   f"extrapolated linearly to {layers} layers; {full * 1e3:.0f} ms per full step"),
+        "sample": (f"{len(runs)} whole steps of the CPU port (oracle/talker_step.py): host planner, all {layers} "
+                   f"decoder layers for all {BATCH} rows (fp32 math, bf16-rounded activations), head and the "
+                   f"reference CPU sampler; {per_step:.2f} s per step"),
     }
 
 
+# Wall-clock budget of the reference arm's timed steps.  Each step is a whole CPU step (seconds); a request for
+# more steps than fit is cut to the number that fits and the line says so.
+REFERENCE_BUDGET_S = 180.0
+
+
 def run_reference(args, world, rank):
+    """The reference arm: the CPU port of the whole step on the host cores, rank 0 only."""
+
     if rank != 0:
         return
-    from oracle.talker_step import CpuTalkerStep
-
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    step = CpuTalkerStep(contexts=contexts_for(0), num_layers=args.layers)
+    step, threads = _cpu_port(args.layers)
     for _ in range(args.warmup):
-        step.time_step(layers=1)
-    probe = step.time_step(layers=1)["layers_s"] + 1e-3
-    # bound the whole run to a few minutes: sample rows when K steps of one layer would take too long
-    rows = BATCH
-    if probe * args.steps > 150.0:
-        rows = max(8, int(BATCH * 150.0 / (probe * args.steps)))
-    times = [step.time_step(rows=rows, layers=1)["full_step_s"] for _ in range(args.steps)]
+        step.time_step(layers=2)  # untimed warm-up steps run 2 of the layers to bound the run
+    first = step.time_step()["step_s"]
+    steps = max(1, min(args.steps, int(REFERENCE_BUDGET_S / first)))
+    times = [first] + [step.time_step()["step_s"] for _ in range(steps - 1)]
     per_step = statistics.mean(times)
     value = BATCH / per_step
+    sample = (f"each step: the whole CPU step - host planner, all {args.layers} decoder layers for all {BATCH} rows "
+              f"(fp32 math, bf16-rounded activations), head and the reference CPU sampler; {threads} threads")
+    if steps < args.steps:
+        sample += f"; {steps} of the {args.steps} requested steps timed ({REFERENCE_BUDGET_S:.0f} s budget)"
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": value,
         "unit": UNIT,
         "n_gpus": world,
-        "steps": args.steps,
+        "steps": steps,
         "warmup": args.warmup,
         "ms_per_step": per_step * 1e3,
         "higher_is_better": True,
@@ -218,10 +233,8 @@ def run_reference(args, world, rank):
         "data": "synthetic (random-init weights, N(0,1) KV, seeded ragged contexts)",
         "config": {"workload": "BASELINE config 2: talker decode step, B=64, ctx U[64,2048], 28 layers, "
                                "P=16, 512k-token pool", "global_batch": BATCH, "seq_len": CTX_HI,
-                   "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"each step: host planner for {BATCH} rows, 1 of {args.layers} layers and head + "
-                                   f"sampler for {rows} rows (fp32, CPU port), extrapolated to the full step"},
+                   "parallelism": "cpu (one host process at every N)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -496,10 +509,61 @@ def run_cp(args, world, rank, local) -> None:
         dist.destroy_process_group()
 
 
-def run_sampler(args, world, rank, local) -> None:
-    """The fused sampler's HBM roofline: the talker sampling of 256 decode steps of B=64 stacked into one
+class SamplerWorkload:
+    """The fused sampler's HBM roofline case: the talker sampling of 256 decode steps of B=64 stacked into one
     16384-row launch (V 3072, bf16 logits, seen mask with 64 ids per row, penalty 1.05, T 0.9, top-k 50,
     top-p 0.95).  Two logits/seen buffer sets alternate so consecutive launches miss L2."""
+
+    ROWS, VOCAB = 256 * BATCH, 3072
+
+    def __init__(self, nqt, dev, seed: int) -> None:
+        self.nqt = nqt
+        rows, vocab = self.ROWS, self.VOCAB
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.sets = []
+        for _ in range(2):
+            logits = (torch.randn(rows, vocab, generator=g, device=dev) * 2.0).to(torch.bfloat16)
+            seen = torch.zeros(rows, vocab, dtype=torch.bool, device=dev)
+            seen.scatter_(1, torch.randint(0, vocab, (rows, 64), generator=g, device=dev), True)
+            self.sets.append((logits, seen))
+        self.temp = torch.full((rows,), 0.9, device=dev)
+        self.top_k = torch.full((rows,), 50, dtype=torch.int32, device=dev)
+        self.top_p = torch.full((rows,), 0.95, device=dev)
+        self.pen = torch.full((rows,), 1.05, device=dev)
+        self.seed = torch.arange(rows, device=dev)
+        self.offset = torch.zeros(rows, dtype=torch.long, device=dev)
+        self.out = torch.empty(rows, dtype=torch.long, device=dev)
+        # algorithmic bytes: logits + seen mask read, tokens written
+        self.bytes_per_launch = rows * vocab * (2 + 1) + rows * 8
+
+    def launch(self, i: int) -> None:
+        logits, seen = self.sets[i & 1]
+        self.nqt.sample_rows(logits, self.temp, self.top_k, self.top_p, self.seed, self.offset,
+                             repetition_penalty=self.pen, seen_token_mask=seen, out=self.out)
+
+    def time_ms(self, steps: int, warmup: int, stream) -> float:
+        for i in range(warmup):
+            self.launch(i)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(steps):
+            self.launch(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / steps
+
+    def roofline(self, ms: float) -> dict:
+        peak, peak_kind = peaks()
+        achieved = self.bytes_per_launch / (ms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": None, "kernel": "sample_kernel", "bytes_per_launch": self.bytes_per_launch,
+                "us_per_launch": ms * 1e3, "rows_per_launch": self.ROWS,
+                "peak_source": f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"}
+
+
+def run_sampler(args, world, rank, local) -> None:
+    """The fused sampler's HBM roofline (SamplerWorkload) as its own bench line."""
 
     from importlib import import_module
 
@@ -507,59 +571,31 @@ def run_sampler(args, world, rank, local) -> None:
     lib_mod = import_module("nari-qwen3-tts_b200._lib")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    rows, vocab = 256 * BATCH, 3072
-    g = torch.Generator(device=dev).manual_seed(4000 + rank)
-    sets = []
-    for _ in range(2):
-        logits = (torch.randn(rows, vocab, generator=g, device=dev) * 2.0).to(torch.bfloat16)
-        seen = torch.zeros(rows, vocab, dtype=torch.bool, device=dev)
-        seen.scatter_(1, torch.randint(0, vocab, (rows, 64), generator=g, device=dev), True)
-        sets.append((logits, seen))
-    temp = torch.full((rows,), 0.9, device=dev)
-    top_k = torch.full((rows,), 50, dtype=torch.int32, device=dev)
-    top_p = torch.full((rows,), 0.95, device=dev)
-    pen = torch.full((rows,), 1.05, device=dev)
-    seed = torch.arange(rows, device=dev)
-    offset = torch.zeros(rows, dtype=torch.long, device=dev)
-    out = torch.empty(rows, dtype=torch.long, device=dev)
-
-    def launch(i):
-        logits, seen = sets[i & 1]
-        nqt.sample_rows(logits, temp, top_k, top_p, seed, offset, repetition_penalty=pen, seen_token_mask=seen,
-                        out=out)
-
+    work = SamplerWorkload(nqt, dev, 4000 + rank)
+    rows = work.ROWS
     for i in range(args.warmup):
-        launch(i)
+        work.launch(i)
     torch.cuda.synchronize()
     lib_mod.reset_launch_count()
     stream = torch.cuda.current_stream(dev)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clocks:
         barrier(world)
         torch.cuda.synchronize()
-        start.record(stream)
-        for i in range(args.steps):
-            launch(i)
-        end.record(stream)
-        torch.cuda.synchronize()
+        ms = work.time_ms(args.steps, 0, stream)
         barrier(world)
     launches = lib_mod.launch_count()
-    ms = max_over_ranks(start.elapsed_time(end), world) / args.steps
-    # algorithmic bytes: logits + seen mask read, tokens written
-    bytes_per = rows * vocab * (2 + 1) + rows * 8
-    achieved = bytes_per / (ms / 1e3) / 1e9
-    peak, peak_kind = peaks()
+    ms = max_over_ranks(ms, world)
     # e2e: the same launch from pinned host logits (H2D inside the timed region) and tokens read back
-    host_logits = sets[0][0].cpu().pin_memory()
+    host_logits = work.sets[0][0].cpu().pin_memory()
     host_tokens = torch.empty(rows, dtype=torch.long).pin_memory()
     e_steps = max(5, args.steps // 4)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(e_steps):
-        sets[0][0].copy_(host_logits, non_blocking=True)
-        launch(0)
-        host_tokens.copy_(out, non_blocking=True)
+        work.sets[0][0].copy_(host_logits, non_blocking=True)
+        work.launch(0)
+        host_tokens.copy_(work.out, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
     e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e_steps
@@ -577,13 +613,11 @@ def run_sampler(args, world, rank, local) -> None:
         "dtype": "bf16",
         "data": "synthetic (N(0,2) logits, 64 seen ids per row)",
         "config": {"workload": "sampler roofline: 256 talker steps x B=64 stacked, V 3072, penalty 1.05, T 0.9, "
-                               "top-k 50, top-p 0.95, Philox draw", "global_batch": world * rows, "seq_len": vocab,
-                   "parallelism": f"dp{world}", "l2": "two 151 MB input sets alternate (> L2)"},
+                               "top-k 50, top-p 0.95, Philox draw", "global_batch": world * rows,
+                   "seq_len": work.VOCAB, "parallelism": f"dp{world}", "l2": "two 151 MB input sets alternate (> L2)"},
         "e2e": {"value": world * rows / (e_ms / 1e3), "unit": "rows/s",
                 "h2d_bytes_per_step": host_logits.numel() * 2, "d2h_bytes_per_step": rows * 8},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "kernel": "sample_kernel", "bytes_per_launch": bytes_per,
-                     "us_per_launch": ms * 1e3, "peak_source": f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"},
+        "roofline": work.roofline(ms),
         "gpu_launches": launches,
         "clocks": clocks.summary(),
         "device_status": nqt.kernels.read_status(dev),
@@ -703,6 +737,12 @@ def main() -> None:
     # DRAM traffic of one decode launch from an ncu capture of this kernel on the same contexts
     # (2-layer model, Sum(ctx + 2) = 74466 tokens): 307.88 MB read + 4.19 MB written, scaled by tokens
     traffic = (307.876352e6 + 4.194816e6) * (sum(lengths) / 74466.0) if args.layers == 28 else None
+
+    # ---------------------------------------------------------------- sampler roofline (same process)
+    sampler = SamplerWorkload(nqt, dev, 4000 + rank)
+    sampler_ms = max_over_ranks(sampler.time_ms(20, 3, stream), world)
+    sampler_line = sampler.roofline(sampler_ms)
+    del sampler
     status = nqt.kernels.read_status(dev) | int(step.planner.status.item())
 
     line = {
@@ -732,9 +772,12 @@ def main() -> None:
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
                 "d2h_bytes_per_step": BATCH * 8},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "kernel": "decode attention (decode_kernel, fused split fix-up)",
+                     "traffic": traffic, "traffic_source": "scaled_from_profile: ncu DRAM bytes of one launch "
+                     "on the same contexts (2-layer capture), scaled by the tokens read",
+                     "kernel": "decode attention (decode_kernel, fused split fix-up)",
                      "bytes_per_launch": attn_bytes, "us_per_launch": attn_ms * 1e3,
                      "peak_source": f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"},
+        "sampler_roofline": sampler_line,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
         "device_status": status,

@@ -49,6 +49,7 @@ extern "C" {
 
 /* nqt_decode_attention_ex flags */
 #define NQT_DECODE_OVERLAP_KV_WRITE 0x1 /* see nqt_decode_attention_ex */
+#define NQT_DECODE_SHORT_WAIT 0x2       /* test only: see nqt_decode_attention_ex */
 
 /* element types */
 #define NQT_BF16 0
@@ -156,6 +157,12 @@ int nqt_decode_attention(
  * kernel writes none of the former, e.g. when it is
  * nqt_qk_norm_rope_paged_kv_write of one decode token per row (that token
  * lies in its row's last tile), or another decode launch on the same plan.
+ * NQT_DECODE_SHORT_WAIT (for tests of the failure path only): every wait of
+ * the launch's TMA pipeline gives up at once instead of after 2 s, so the
+ * launch reports NQT_DEV_TIMEOUT and its output is undefined.  A launch
+ * whose wait gave up still settles its split-KV fix-up state and waits for
+ * its own copies in flight before exiting, so the next launch on the same
+ * plan is correct.
  */
 int nqt_decode_attention_ex(
     const void* q, int64_t q_stride_tok, int64_t q_stride_head,
@@ -180,7 +187,9 @@ int nqt_decode_attention_ex(
  * larger shapes return NQT_ERR_CAPACITY (see nqt_last_error).
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make it before any
- * stream capture.  All calls share the array: calls that may overlap on
+ * stream capture.  The looked-up address belongs to the device's primary
+ * context: after a cudaDeviceReset of that device, do not call this entry
+ * point on it again in the same process.  All calls share the array: calls that may overlap on
  * the GPU (other streams or threads on the same device) race and must be
  * serialised by the caller.  Inputs, outputs and status as in
  * nqt_decode_attention.

@@ -118,16 +118,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait on an mbarrier phase.  Returns false (and reports a timeout)
 // when the phase did not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, int32_t* status, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - start > kWaitLimitNs) {
+    if (global_timer_ns() - start > limit_ns) {
       report(status, NQT_DEV_TIMEOUT);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {
+  return mbar_wait_ns(bar, parity, status, kWaitLimitNs);
 }
 
 // 4-D tiled TMA load into shared memory, completing on `bar`.

@@ -79,6 +79,7 @@ struct DecodeArgs {
   int batch, hq, hkv, group, page_size, total_pages, n_ctas;
   int early;  // NQT_DECODE_OVERLAP_KV_WRITE: read the plan and older tiles before the dependency wait
   float scale_log2;
+  uint64_t wait_ns;  // limit of the pipeline's mbarrier waits (kWaitLimitNs unless NQT_DECODE_SHORT_WAIT)
 };
 
 // ------------------------------------------------------------------ plan
@@ -247,6 +248,34 @@ __device__ __forceinline__ void fixup_sequence(const DecodeArgs& p, int seq, int
   }
 }
 
+// Count a split segment this warp gave up on in on its ticket (see the abandon path in decode_kernel).
+__device__ __forceinline__ void abandon_ticket(const DecodeArgs& p, int64_t total, int n, int64_t t_begin,
+                                               int64_t t_end, int seq, int seq_t0, int seq_t1, int kvh, int lane) {
+  if (t_begin <= seq_t0 && t_end >= seq_t1) return;  // a whole sequence has no ticket
+  const int c0 = owner_cta(total, n, seq_t0);
+  const int c1 = owner_cta(total, n, seq_t1 - 1);
+  int32_t* ticket = p.tickets + static_cast<int64_t>(seq) * p.hq + kvh;
+  int arrived = 0;
+  if (lane == 0) arrived = atomic_add_acq_rel_gpu(ticket, 1);
+  arrived = __shfl_sync(kFull, arrived, 0);
+  if (arrived == c1 - c0 && lane == 0) *ticket = 0;
+}
+
+// Last step of every warp of a decode CTA.  When a wait gave up, TMA copies of tiles that were issued
+// but not consumed may still be landing in this CTA's shared memory; one thread waits for them (with
+// the full limit) before the CTA exits, so no copy completes into memory the CTA has given back.
+template <int STAGES>
+__device__ __forceinline__ void drain_and_exit(uint64_t* full, const int& s_issued, const int* s_progress,
+                                               int consumers, int n_tiles, int32_t* status) {
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  int lo = n_tiles;
+  for (int w = 0; w < consumers; ++w) lo = s_progress[w] < lo ? s_progress[w] : lo;
+  // a tile j in [lo, issued) is not consumed by every warp, so tile j + STAGES was never issued and
+  // the parity of phase j / STAGES identifies tile j's copy
+  for (int j = lo; j < s_issued; ++j) mbar_wait(&full[j % STAGES], (j / STAGES) & 1, status);
+}
+
 constexpr int kSmemPrefix = 1024;  // tile_indptr entries staged in shared memory (batch + 1 <= this)
 constexpr int kSmemPages = 1024;   // page ids of one CTA's tile range staged in shared memory
 
@@ -269,6 +298,10 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   uint64_t* empty = full + STAGES;
   int32_t* s_prefix = reinterpret_cast<int32_t*>(empty + STAGES);
   int32_t* s_pages = s_prefix + kSmemPrefix;
+  // tiles the producer issued and, per consumer warp, the first tile it did not consume: after a wait
+  // gave up, the CTA waits for the copies still in flight before it exits
+  __shared__ int s_issued;
+  __shared__ int s_progress[HPC];
 
   // Launched with programmatic serialization; the next kernel may be scheduled as soon as every CTA
   // here has started.  By default everything waits for the previous grid.  With `early` the caller
@@ -338,6 +371,7 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
     int seq_t1 = prefix[seq + 1];
     int seq_base = p.indptr[seq];
     bool dependency_met = !p.early;
+    int issued = 0;
     for (int i = 0; i < n_tiles; ++i) {
       const int64_t t = t_begin + i;
       while (t >= seq_t1) {  // advance to the owning sequence (skips empty rows)
@@ -352,7 +386,7 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
       }
       const int s = i % STAGES;
       // warp-uniform decision: every lane reaches the same __syncwarp
-      const bool ready = i < STAGES || mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, p.status);
+      const bool ready = i < STAGES || mbar_wait_ns(&empty[s], ((i / STAGES) - 1) & 1, p.status, p.wait_ns);
       if (!__all_sync(kFull, ready)) break;
       const int in_seq = static_cast<int>(t - seq_t0);
       const int page_local = in_seq / tpp;
@@ -368,7 +402,10 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
       if (lane < HPC * kHalves)
         tma_load_4d_hint(smem + s * Cfg::kStageBytes + (box_h * kHalves + box_half) * kBoxBytes, &tmap, &full[s],
                          box_half * 64, kv0 + box_h, tile_in_page * kTok, page * 2, evict_first);
+      issued = i + 1;
     }
+    if (lane == 0) s_issued = issued;
+    drain_and_exit<STAGES>(full, s_issued, s_progress, HPC, n_tiles, p.status);
     return;
   }
 
@@ -388,6 +425,7 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
   int seq_t1 = prefix[seq + 1];
   bool seg_open = false;
   int fix_a = -1, fix_b = -1;  // split sequences whose ticket this warp completed
+  int stop = n_tiles;          // first tile this warp did not consume (n_tiles unless a wait gave up)
 
   // ldmatrix lane roles
   const int lm_j = lane >> 3;
@@ -430,7 +468,10 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
     }
 
     const int s = i % STAGES;
-    if (!mbar_wait(&full[s], (i / STAGES) & 1, p.status)) return;
+    if (!__all_sync(kFull, mbar_wait_ns(&full[s], (i / STAGES) & 1, p.status, p.wait_ns))) {
+      stop = i;
+      break;
+    }
     uint8_t* head_box = smem + s * Cfg::kStageBytes + warp * kHalves * kBoxBytes;
 
     if (valid < kTok) {
@@ -585,6 +626,16 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
     }
   }
 
+  if (stop < n_tiles) {
+    // A wait gave up (NQT_DEV_TIMEOUT is set and this launch's output is undefined).  The split
+    // segments this warp did not finish still count in on their tickets, so every ticket of the
+    // launch completes and returns to zero: later launches on the same plan stay correct.  Only a
+    // range's first and last segments can be split; the open one is the segment of tile `stop`.
+    abandon_ticket(p, total, n, t_begin, t_end, seq, seq_t0, seq_t1, kvh, lane);
+    const int last = find_seq(prefix, p.batch, t_end - 1);
+    if (last != seq) abandon_ticket(p, total, n, t_begin, t_end, last, prefix[last], prefix[last + 1], kvh, lane);
+  }
+
   // deferred fix-ups: the accumulators are dead here, so the combine does not raise the register
   // footprint of the tile loop
   __syncwarp();
@@ -604,6 +655,8 @@ __global__ void __launch_bounds__((HPC + 1) * 32) decode_kernel(const __grid_con
     else
       fixup_sequence<D, 8>(p, fs, kvh, total, n, c0, c1, f_t0, lane);
   }
+  if (lane == 0) s_progress[warp] = stop;
+  drain_and_exit<STAGES>(full, s_issued, s_progress, HPC, n_tiles, p.status);
 }
 
 // ------------------------------------------------------------------ host
@@ -726,7 +779,7 @@ int run_decode(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const
                int total_pages, int page_size, const int32_t* kv_indptr, const int32_t* kv_indices,
                const int32_t* last_page_len, int batch, int num_qo_heads, int num_kv_heads, int head_dim,
                float sm_scale, void* out, int64_t out_stride_tok, int64_t out_stride_head, uint8_t* base,
-               const WsLayout& w, int max_ctas, int early, int32_t* status, cudaStream_t s) {
+               const WsLayout& w, int max_ctas, int early, int short_wait, int32_t* status, cudaStream_t s) {
   CUtensorMap map;
   int rc = encode_layer_map(&map, layer_cache, total_pages, page_size, num_kv_heads, head_dim);
   if (rc != NQT_OK) return rc;
@@ -755,6 +808,7 @@ int run_decode(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const
   a.n_ctas = 1;
   a.early = early;
   a.scale_log2 = sm_scale * 1.4426950408889634f;
+  a.wait_ns = short_wait ? 0 : kWaitLimitNs;
   return head_dim == 128 ? dispatch_hpc<128>(map, a, max_ctas, s) : dispatch_hpc<64>(map, a, max_ctas, s);
 }
 
@@ -772,13 +826,14 @@ extern "C" int nqt_decode_attention_ex(const void* q, int64_t q_stride_tok, int6
                              num_kv_heads, head_dim);
   if (rc != NQT_OK) return rc;
   if (!workspace || batch > batch_capacity) return NQT_ERR_ARG;
-  if (flags & ~NQT_DECODE_OVERLAP_KV_WRITE) return NQT_ERR_ARG;
+  if (flags & ~(NQT_DECODE_OVERLAP_KV_WRITE | NQT_DECODE_SHORT_WAIT)) return NQT_ERR_ARG;
   const WsLayout w = ws_layout(batch_capacity, num_qo_heads, head_dim);
   if (workspace_bytes < w.total) return NQT_ERR_CAPACITY;
   return run_decode(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr, kv_indices,
                     last_page_len, batch, num_qo_heads, num_kv_heads, head_dim, sm_scale, out, out_stride_tok,
                     out_stride_head, static_cast<uint8_t*>(workspace), w, kMaxSplitCtas,
-                    (flags & NQT_DECODE_OVERLAP_KV_WRITE) ? 1 : 0, status, as_stream(stream));
+                    (flags & NQT_DECODE_OVERLAP_KV_WRITE) ? 1 : 0, (flags & NQT_DECODE_SHORT_WAIT) ? 1 : 0,
+                    status, as_stream(stream));
 }
 
 extern "C" int nqt_decode_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
@@ -810,7 +865,10 @@ extern "C" int nqt_decode_attention(const void* q, int64_t q_stride_tok, int64_t
 // the name is a stand-in, not the device buffer), so the address is looked
 // up once per device with cudaGetSymbolAddress, with that device current,
 // on the first call made on it; make that first call before any stream
-// capture.  Nothing in the array has to start at zero: each call rewrites
+// capture.  The address stays valid for the life of the device's primary
+// context: a caller that resets the device (cudaDeviceReset) must not call
+// this entry point on that device again in the same process, because the
+// cached address belongs to the destroyed context.  Nothing in the array has to start at zero: each call rewrites
 // the plan before the attention kernels read it.  All calls share the
 // array, so two calls that can overlap on the GPU (different streams, or
 // different threads on one device) race on it; serialise them.
@@ -839,7 +897,10 @@ int noalloc_scratch(uint8_t** out) {
     set_last_error("nqt_decode_attention_noalloc: cudaGetDevice", err);
     return NQT_ERR_CUDA;
   }
-  if (dev < 0 || dev >= kMaxDevices) return NQT_ERR_UNSUPPORTED;
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_last_message("nqt_decode_attention_noalloc: device ordinal beyond the 64 devices this library tracks");
+    return NQT_ERR_UNSUPPORTED;
+  }
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (g_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
@@ -887,5 +948,5 @@ extern "C" int nqt_decode_attention_noalloc(const void* q, int64_t q_stride_tok,
   if (rc != NQT_OK) return rc;
   return run_decode(q, q_stride_tok, q_stride_head, layer_cache, total_pages, page_size, kv_indptr, kv_indices,
                     last_page_len, batch, num_qo_heads, num_kv_heads, head_dim, sm_scale, out, out_stride_tok,
-                    out_stride_head, base, w, kNoAllocMaxCtas, 0, status, s);
+                    out_stride_head, base, w, kNoAllocMaxCtas, 0, 0, status, s);
 }

@@ -10,13 +10,23 @@ capture kinds: metadata with ``qo_indptr`` is a ragged causal prefill,
 without it a one-query decode (the two reference classes,
 FlashInferPrefillBinding :140-226 and FlashInferDecodeBinding :229-306).
 
+The factory is called with the same arguments for both kinds, so a binding
+takes its kind from its first ``plan``: after that, prefill metadata on a
+decode binding raises the reference decode binding's ValueError and decode
+metadata on a prefill binding the reference prefill binding's.
+
 Differences by design:
   * ``plan`` accepts host (pinned) or device metadata.  It copies it into
     the static buffers on the current stream and builds the split-KV
     partition on the device, so there is no host plan, no signature cache
-    and nothing to invalidate; plan reuse is always on.
-  * each binding owns its split-KV workspace, so bindings that share the
-    reference's per-slot workspace cannot overwrite each other's plan.
+    and nothing to invalidate: every ``plan`` rewrites the partition.
+  * the split-KV plan and partials live at the start of the factory's
+    per-slot ``workspace`` (the buffer the reference hands FlashInfer).
+    Bindings of one slot share it the way the reference's do: a binding's
+    ``plan`` must come before its replay, which the executor already does
+    (executor/talker.py plans before every replay).  Without a workspace, or
+    with one smaller than ``nqt_decode_workspace_bytes`` (about 10.6 MB at
+    64 rows, 16 heads, D 128), the binding allocates its own.
 """
 
 from __future__ import annotations
@@ -30,8 +40,9 @@ from . import _lib
 from ._lib import call, ptr
 from .kernels import device_status, paired_qk_norm_rope_paged_cache_
 
-# nqt_decode_attention_ex flag (include/nqt.h NQT_DECODE_OVERLAP_KV_WRITE)
+# nqt_decode_attention_ex flags (include/nqt.h NQT_DECODE_OVERLAP_KV_WRITE, NQT_DECODE_SHORT_WAIT)
 DECODE_OVERLAP_KV_WRITE = 0x1
+DECODE_SHORT_WAIT = 0x2
 
 
 @dataclass(frozen=True, slots=True)
@@ -74,6 +85,7 @@ def batch_decode_paged(
     out: torch.Tensor | None = None,
     plan: bool = True,
     overlap_kv_write: bool = False,
+    short_wait: bool = False,
 ) -> torch.Tensor:
     """Paged GQA decode attention, one query per row (FlashInfer decode
     wrapper semantics: all (n_pages - 1) * P + last_page_len tokens).
@@ -82,7 +94,11 @@ def batch_decode_paged(
     no KV tile but each row's last, and neither the page table nor the plan
     (the one-token-per-row K/V write of a decode step, or another decode
     launch on the same plan); the decode kernel then stages page ids and
-    streams the older tiles while that kernel finishes."""
+    streams the older tiles while that kernel finishes.
+
+    ``short_wait`` exists for failure-path tests only: the launch's pipeline
+    waits give up at once, it reports NQT_DEV_TIMEOUT and its output is
+    undefined, but the plan stays usable for the next launch."""
 
     rows, hq, d = query.shape
     pages, kinds, page_size, hkv, d2 = layer_cache.shape
@@ -113,7 +129,7 @@ def batch_decode_paged(
         ptr(out), out.stride(0), out.stride(1),
         ptr(workspace), workspace.numel() * workspace.element_size(),
         # a plan made just above is the previous kernel: it must be complete before anything is read
-        DECODE_OVERLAP_KV_WRITE if overlap_kv_write and not plan else 0,
+        (DECODE_OVERLAP_KV_WRITE if overlap_kv_write and not plan else 0) | (DECODE_SHORT_WAIT if short_wait else 0),
         ptr(device_status(device)), stream,
     )
     return out
@@ -182,8 +198,14 @@ class B200TalkerBinding:
         dtype: torch.dtype,
         slot: int | None = None,
         metadata: TalkerAttentionMetadata | None = None,
+        mode: str | None = None,
     ) -> None:
+        """``mode`` ("decode" or "prefill") fixes the binding's kind up front;
+        by default the first ``plan`` fixes it."""
+
         del shared_plan_state, slot  # no shared host plan: see the module docstring
+        if mode not in (None, "decode", "prefill"):
+            raise ValueError("mode must be 'decode', 'prefill' or None")
         device = torch.device(device)
         if device.type != "cuda":
             raise ValueError("B200TalkerBinding requires a CUDA device")
@@ -209,9 +231,15 @@ class B200TalkerBinding:
         self.paged_kv_indices = torch.zeros(total_pages + capture_batch_size, dtype=torch.int32, device=device)
         self.paged_kv_last_page_len = torch.ones(capture_batch_size, dtype=torch.int32, device=device)
         nbytes = _lib.lib().nqt_decode_workspace_bytes(capture_batch_size, num_qo_heads, head_dim)
-        self.decode_workspace = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        if mode == "prefill":
+            self.decode_workspace = torch.empty(0, dtype=torch.uint8, device=device)
+        elif workspace is not None and workspace.is_contiguous() and workspace.numel() >= nbytes:
+            self.decode_workspace = workspace[:nbytes]
+        else:
+            self.decode_workspace = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         self.metadata: TalkerAttentionMetadata | None = None
-        self._prefill = False
+        self._mode = mode
+        self._prefill = mode == "prefill"
         self._layer_index = 0
         if metadata is not None:
             self.plan(metadata)
@@ -225,6 +253,7 @@ class B200TalkerBinding:
         if metadata.paged_kv_indptr.shape != self.paged_kv_indptr.shape:
             raise ValueError("Talker page metadata does not match the captured batch size")
         prefill = metadata.qo_indptr is not None
+        self._fix_mode(prefill)
         with torch.cuda.device(self.device):
             self._copy(self.position_ids, metadata.position_ids)
             self._copy(self.write_pages, metadata.write_pages)
@@ -238,6 +267,15 @@ class B200TalkerBinding:
             self._prefill = prefill
             self.metadata = metadata
             self.device_plan()
+
+    def _fix_mode(self, prefill: bool) -> None:
+        # the reference bindings' checks (executor/talker_kv.py:176-177, 260-261)
+        if self._mode == "decode" and prefill:
+            raise ValueError("Talker decode cannot contain packed query metadata")
+        if self._mode == "prefill" and not prefill:
+            raise ValueError("Talker prefill requires packed query metadata")
+        if self._mode is None:
+            self._mode = "prefill" if prefill else "decode"
 
     def device_plan(self) -> None:
         """Build the split-KV partition from the staged buffers (device only)."""
@@ -257,6 +295,7 @@ class B200TalkerBinding:
         """Mark the static buffers (written in place by the GPU planner) as
         this step's metadata, without copies."""
 
+        self._fix_mode(prefill)
         self._prefill = prefill
         self.metadata = TalkerAttentionMetadata(
             qo_indptr=self.qo_indptr if prefill else None,

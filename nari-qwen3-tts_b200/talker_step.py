@@ -149,7 +149,8 @@ class TalkerDecodeStep:
                                          num_qo_heads=s.num_heads, head_dim=s.head_dim)
         self.binding = B200TalkerBinding(storage=self.storage, capture_batch_size=batch, token_capacity=batch,
                                          num_qo_heads=s.num_heads, num_kv_heads=s.num_kv_heads, head_dim=s.head_dim,
-                                         page_size=page_size, total_pages=total_pages, device=dev, dtype=bf16)
+                                         page_size=page_size, total_pages=total_pages, device=dev, dtype=bf16,
+                                         mode="decode")
         # static step buffers (graph inputs and outputs)
         self.hidden_in = torch.zeros(batch, s.hidden, dtype=bf16, device=dev)
         self.temperature = torch.full((batch,), 0.9, device=dev)
@@ -165,6 +166,8 @@ class TalkerDecodeStep:
         self._act = torch.empty(batch, s.ffn, dtype=bf16, device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
         self.contexts: list[int] = []
+        # parity hook: Exp(1) noise [batch, vocab] for the sampler's noise entry instead of the Philox draw
+        self.sample_noise: torch.Tensor | None = None
         # pinned host staging for step()
         self._h_hidden = torch.empty(batch, s.hidden, dtype=bf16).pin_memory()
         self._h_tokens = torch.empty(batch, dtype=torch.long).pin_memory()
@@ -196,7 +199,11 @@ class TalkerDecodeStep:
         self.seen.scatter_(1, ids.to(self.device), True)
 
     # ---------------------------------------------------------------- step body
-    def forward(self) -> torch.Tensor:
+    def forward(self, trace: list | None = None) -> torch.Tensor:
+        """The step body (what capture() records).  ``trace``, for parity
+        tests of an eager step: receives (normed input, residual) before the
+        first layer and after every layer, then the logits."""
+
         s = self.shape
         b = self.binding
         self.planner.plan(b, prefill=False)
@@ -206,6 +213,8 @@ class TalkerDecodeStep:
         kernels.rmsnorm(self.hidden_in, w.ln_in[0], s.eps, out=x)
         hq, hkv, d = s.num_heads, s.num_kv_heads, s.head_dim
         rows = self.batch
+        if trace is not None:
+            trace.append((x.clone(), residual.clone()))
         for layer in range(s.num_layers):
             b.select_layer(layer)
             qkv = F.linear(x, w.w_qkv[layer])
@@ -215,10 +224,14 @@ class TalkerDecodeStep:
             attn = b.attend(w.attn[layer], q, k, v)
             o = F.linear(attn.view(rows, hq * d), w.w_o[layer])
             x = _mlp_block(w, s, layer, o, residual, self._act)
+            if trace is not None:
+                trace.append((x.clone(), residual.clone()))
         logits = F.linear(x, w.w_head)
+        if trace is not None:
+            trace.append(logits.clone())
         sample_rows(logits, self.temperature, self.top_k, self.top_p, self.seed, self.offset,
                     repetition_penalty=self.penalty, seen_token_mask=self.seen, update_seen=True,
-                    round_scaled_to_input=False, out=self.tokens)
+                    round_scaled_to_input=False, noise=self.sample_noise, out=self.tokens)
         self.planner.commit(self.publish)
         self.offset.add_(FRAME_OFFSET_STRIDE)
         return self.tokens
@@ -310,8 +323,10 @@ class TalkerMixedStep:
         self.adm = self.dec.view(capture_rows=churn_rows, token_capacity=0)
         common = dict(storage=self.storage, num_qo_heads=s.num_heads, num_kv_heads=s.num_kv_heads,
                       head_dim=s.head_dim, page_size=P, total_pages=total_pages, device=dev, dtype=torch.bfloat16)
-        self.pre_b = B200TalkerBinding(capture_batch_size=self.n_pre, token_capacity=self.t_pre, **common)
-        self.dec_b = B200TalkerBinding(capture_batch_size=self.n_dec, token_capacity=self.n_dec, **common)
+        self.pre_b = B200TalkerBinding(capture_batch_size=self.n_pre, token_capacity=self.t_pre, mode="prefill",
+                                       **common)
+        self.dec_b = B200TalkerBinding(capture_batch_size=self.n_dec, token_capacity=self.n_dec, mode="decode",
+                                       **common)
         # allocation-only metadata sink of the admission step
         self._adm_indptr = torch.zeros(churn_rows + 1, dtype=torch.int32, device=dev)
         self._adm_indices = torch.zeros(total_pages + churn_rows, dtype=torch.int32, device=dev)
@@ -337,6 +352,8 @@ class TalkerMixedStep:
         self.seen = torch.zeros(n, s.vocab, dtype=torch.bool, device=dev)
         self.out_tokens = torch.zeros(n, dtype=torch.long, device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
+        # parity hook: Exp(1) noise [rows, vocab] for the sampler's noise entry instead of the Philox draw
+        self.sample_noise: torch.Tensor | None = None
 
     def admit(self, *, scatter_seed: int = 0) -> None:
         """Prefill rows start empty; decode rows get their contexts on scattered pages."""
@@ -359,7 +376,10 @@ class TalkerMixedStep:
         self.seen.zero_()
         self.seen.scatter_(1, ids.to(self.device), True)
 
-    def forward(self) -> torch.Tensor:
+    def forward(self, trace: list | None = None) -> torch.Tensor:
+        """The step body; ``trace`` as in TalkerDecodeStep.forward (over all
+        packed tokens, prefill chunks first)."""
+
         s, w = self.shape, self.weights
         hq, hkv, d = s.num_heads, s.num_kv_heads, s.head_dim
         tp, nd, T = self.t_pre, self.n_dec, self.tokens
@@ -368,6 +388,8 @@ class TalkerMixedStep:
         x, residual = self._x, self._residual
         residual.copy_(self.hidden_in)
         kernels.rmsnorm(self.hidden_in, w.ln_in[0], s.eps, out=x)
+        if trace is not None:
+            trace.append((x.clone(), residual.clone()))
         for layer in range(s.num_layers):
             cache = self.storage[layer]
             qkv = F.linear(x, w.w_qkv[layer])
@@ -388,10 +410,14 @@ class TalkerMixedStep:
                                out=attn[tp:], plan=False)
             o = F.linear(self._attn, w.w_o[layer])
             x = _mlp_block(w, s, layer, o, residual, self._act)
+            if trace is not None:
+                trace.append((x.clone(), residual.clone()))
         logits = F.linear(x.index_select(0, self._sample_rows), w.w_head)
+        if trace is not None:
+            trace.append(logits.clone())
         sample_rows(logits, self.temperature, self.top_k, self.top_p, self.seed, self.offset,
                     repetition_penalty=self.penalty, seen_token_mask=self.seen, update_seen=True,
-                    round_scaled_to_input=False, out=self.out_tokens)
+                    round_scaled_to_input=False, noise=self.sample_noise, out=self.out_tokens)
         self.pre.commit(False)
         self.dec.commit(False)
         # churn: churn_rows decode requests finish and new ones of the same lengths are admitted

@@ -1,18 +1,32 @@
-"""CPU port of one talker decode step, timed as the CPU baseline.
+"""CPU port of one talker step: the teacher-forced layer used by the step
+parity tests, and the timed CPU baseline.
 
 The reference has no CPU talker attention (attend() always runs Triton +
 FlashInfer), so its "CPU torch path" for this step is restated here with
 the oracle pieces: the host page allocator and metadata builder
 (oracle/planner.py, = executor/cache.py + executor/talker_kv.py:403-480),
-RMSNorm / QK-norm + RoPE + paged K/V write / paged decode attention in fp32
-(oracle/attention.py), fp32 torch GEMMs for the projections and MLP, and the
-reference CPU sampler semantics (oracle/sampler.py).
+RMSNorm / QK-norm + RoPE + paged K/V write / paged decode and causal
+prefill attention in fp32 (oracle/attention.py), fp32 torch GEMMs for the
+projections and MLP, and the reference CPU sampler semantics
+(oracle/sampler.py).
 
-``CpuTalkerStep.time_step`` runs a bounded sample of the step - the planner,
-``rows`` rows through ``layers`` of the decoder layers and the head +
-sampler - and extrapolates to the full step (all layers, all rows) because
-every term is linear in rows and layers.  Test and baseline infrastructure
-only; the product never imports it.
+``layer_forward`` is one decoder layer in the order of the reference's
+captured step (model/components.py:37-90 with model/layers.py:28-115,
+296-317): QKV projection, attend (QK norm + RoPE + K/V write, attention),
+O projection, fused residual add + post-attention RMSNorm, gate/up,
+SiLU * up, down, fused residual add + the next layer's input RMSNorm.  It
+rounds to bf16 wherever the bf16 step materialises a tensor (each GEMM
+output, the attention output, the residual, each norm output), so a
+teacher-forced comparison with the GPU step sees only accumulation-order and
+attention-tolerance differences.  The fused add + RMSNorm follows FlashInfer's
+fused_add_rmsnorm: the sum is kept in fp32 for the norm and stored to the
+residual rounded.
+
+``CpuTalkerStep.time_step`` runs the whole step - the planner, every
+decoder layer for every row, the head and the sampler - on the host cores.
+Only ``layers_resident`` layers of weights and KV are held (the port cycles
+through them), which changes no arithmetic.  Test and baseline
+infrastructure only; the product never imports it.
 """
 
 from __future__ import annotations
@@ -24,6 +38,76 @@ import torch
 from . import attention as oatt
 from . import planner as oplan
 from . import sampler as osamp
+
+BF16 = torch.bfloat16
+
+
+def _round(x: torch.Tensor) -> torch.Tensor:
+    return x.to(BF16).float()
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """fp32 RMSNorm (model/layers.py:110-115 / flashinfer.norm.rmsnorm), unrounded."""
+
+    xf = x.float()
+    return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float):
+    """(normed bf16, residual bf16) of flashinfer.norm.fused_add_rmsnorm (model/layers.py:42-77)."""
+
+    r = x.float() + residual.float()
+    return _round(rmsnorm(r, w, eps)), _round(r)
+
+
+def layer_forward(x, residual, *, w_qkv, w_o, w_gate_up, w_down, ln_post, ln_next, q_norm, k_norm, eps, theta,
+                  heads, kv_heads, head_dim, cache, meta, prefill_rows=0):
+    """One decoder layer, teacher-forced.
+
+    x: the layer's normed input, residual: the residual stream (both [T, hidden],
+    bf16 values).  cache: the layer view [pages, 2, P, Hkv, D] bf16 (written in
+    place).  meta: dict of CPU tensors for the step's rows - for a decode
+    group ``pos, wp, wo, indptr, indices, last``; with ``prefill_rows`` > 0 the
+    first ``prefill_rows`` tokens form a prefill group described by
+    ``pre_*`` keys (``pre_qo_indptr`` included) and the rest the decode group.
+    Returns (next normed input, residual), bf16 values in fp32 tensors.
+    """
+
+    h, hkv, d = heads, kv_heads, head_dim
+    t = x.shape[0]
+    qkv = _round(x.float() @ w_qkv.float().T)
+    q = qkv[:, : h * d].reshape(t, h, d).to(BF16)
+    k = qkv[:, h * d: (h + hkv) * d].reshape(t, hkv, d).to(BF16)
+    v = qkv[:, (h + hkv) * d:].reshape(t, hkv, d).to(BF16)
+    attn = torch.zeros(t, h, d)
+    groups = []
+    if prefill_rows:
+        groups.append(("pre_", 0, prefill_rows, True))
+    groups.append(("", prefill_rows, t, False))
+    for key, lo, hi, is_prefill in groups:
+        if hi == lo:
+            continue
+        qs, ks = q[lo:hi].clone(), k[lo:hi].clone()
+        oatt.qk_norm_rope_paged_(qs, ks, v[lo:hi], q_norm, k_norm, meta[key + "pos"], eps, theta, cache,
+                                 meta[key + "wp"], meta[key + "wo"])
+        if is_prefill:
+            attn[lo:hi] = oatt.paged_prefill(qs.float(), cache, meta["pre_qo_indptr"], meta["pre_indptr"],
+                                             meta["pre_indices"], meta["pre_last"])
+        else:
+            attn[lo:hi] = oatt.paged_decode(qs.float(), cache, meta["indptr"], meta["indices"], meta["last"])
+    o = _round(_round(attn).reshape(t, h * d) @ w_o.float().T)
+    x2, residual = add_rmsnorm(o, residual, ln_post, eps)
+    gu = _round(x2 @ w_gate_up.float().T)
+    ffn = gu.shape[1] // 2
+    act = _round(torch.nn.functional.silu(gu[:, :ffn]) * gu[:, ffn:])
+    m = _round(act @ w_down.float().T)
+    return add_rmsnorm(m, residual, ln_next, eps)
+
+
+def head_logits(x: torch.Tensor, w_head: torch.Tensor) -> torch.Tensor:
+    """Codec head on the final normed hidden state, rounded to bf16 like the step's GEMM."""
+
+    return _round(x.float() @ w_head.float().T)
 
 
 class CpuTalkerStep:
@@ -60,60 +144,46 @@ class CpuTalkerStep:
         self.seen.scatter_(1, torch.randint(0, vocab, (self.batch, 64), generator=g), True)
         self.offset = torch.zeros(self.batch, dtype=torch.long)
 
-    @staticmethod
-    def _rms(x, w, eps):
-        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+    def _layer(self, layer, x, residual, meta):
+        i = layer % self.layers_resident
+        return layer_forward(x, residual, w_qkv=self.w_qkv[i], w_o=self.w_o[i], w_gate_up=self.w_gu[i],
+                             w_down=self.w_down[i], ln_post=self.norm, ln_next=self.norm, q_norm=self.qk_norm,
+                             k_norm=self.qk_norm, eps=self.eps, theta=self.theta, heads=self.heads,
+                             kv_heads=self.kv_heads, head_dim=self.head_dim, cache=self.cache[i], meta=meta)
 
-    def _layer(self, layer, x, meta, rows):
-        h, hkv, d = self.heads, self.kv_heads, self.head_dim
-        qkv = self._rms(x, self.norm, self.eps) @ self.w_qkv[layer].T
-        q = qkv[:, : h * d].reshape(rows, h, d).to(torch.bfloat16)
-        k = qkv[:, h * d: (h + hkv) * d].reshape(rows, hkv, d).to(torch.bfloat16)
-        v = qkv[:, (h + hkv) * d:].reshape(rows, hkv, d).to(torch.bfloat16)
-        oatt.qk_norm_rope_paged_(q, k, v, self.qk_norm, self.qk_norm, meta["pos"], self.eps, self.theta,
-                                 self.cache[layer], meta["wp"], meta["wo"])
-        attn = oatt.paged_decode(q.float(), self.cache[layer], meta["indptr"], meta["indices"], meta["last"])
-        x = x + attn.reshape(rows, h * d) @ self.w_o[layer].T
-        gu = self._rms(x, self.norm, self.eps) @ self.w_gu[layer].T
-        act = torch.nn.functional.silu(gu[:, : self.ffn]) * gu[:, self.ffn:]
-        return x + act @ self.w_down[layer].T
+    def time_step(self, *, layers: int | None = None) -> dict:
+        """Run one whole step (all rows; ``layers`` decoder layers, by default
+        all of them) and return the seconds spent in each part."""
 
-    def time_step(self, *, rows: int | None = None, layers: int = 1) -> dict:
-        """Run one sampled step; returns the measured parts and the
-        extrapolated full-step seconds."""
-
-        rows = rows or self.batch
+        layers = self.num_layers if layers is None else layers
         rids = [f"r{i}" for i in range(self.batch)]
+        rows = self.batch
         t0 = time.perf_counter()
-        m = self.pool.metadata(rids, [1] * self.batch, self.batch, self.batch, False)
-        t1 = time.perf_counter()
-        sel = slice(0, rows)
-        nsel = m["paged_kv_indptr"][rows]
+        m = self.pool.metadata(rids, [1] * rows, rows, rows, False)
         meta = {
-            "indptr": torch.tensor(m["paged_kv_indptr"][: rows + 1], dtype=torch.int32),
-            "indices": torch.tensor(m["paged_kv_indices"][:nsel], dtype=torch.int32),
-            "last": torch.tensor(m["paged_kv_last_page_len"][sel], dtype=torch.int32),
-            "pos": torch.tensor(m["position_ids"][sel]),
-            "wp": torch.tensor(m["write_pages"][sel]),
-            "wo": torch.tensor(m["write_offsets"][sel]),
+            "indptr": torch.tensor(m["paged_kv_indptr"], dtype=torch.int32),
+            "indices": torch.tensor(m["paged_kv_indices"], dtype=torch.int32),
+            "last": torch.tensor(m["paged_kv_last_page_len"], dtype=torch.int32),
+            "pos": torch.tensor(m["position_ids"]),
+            "wp": torch.tensor(m["write_pages"]),
+            "wo": torch.tensor(m["write_offsets"]),
         }
-        x = torch.randn(rows, self.hidden)
+        t1 = time.perf_counter()
+        residual = _round(torch.randn(rows, self.hidden))
+        x = _round(rmsnorm(residual, self.norm, self.eps))
+        for layer in range(layers):
+            x, residual = self._layer(layer, x, residual, meta)
         t2 = time.perf_counter()
-        for i in range(layers):
-            x = self._layer(i % self.layers_resident, x, meta, rows)
-        t3 = time.perf_counter()
-        logits = self._rms(x, self.norm, self.eps) @ self.w_head.T
+        logits = head_logits(x, self.w_head)
         tokens = osamp.sample_logits(
             logits, torch.full((rows,), 0.9), torch.full((rows,), 50, dtype=torch.int32), torch.full((rows,), 0.95),
-            torch.arange(rows), self.offset[sel], repetition_penalty=torch.full((rows,), 1.05),
-            seen_token_mask=self.seen[sel])
+            torch.arange(rows), self.offset, repetition_penalty=torch.full((rows,), 1.05),
+            seen_token_mask=self.seen)
         self.seen[torch.arange(rows), tokens] = True
-        t4 = time.perf_counter()
-        # discard the reservation so every sampled step sees the same lengths (a stationary sample)
+        t3 = time.perf_counter()
+        # discard the reservation so every step sees the same lengths (a stationary workload)
         for rid in rids:
             self.pool.discard(rid)
         self.offset += 512
-        scale_rows = self.batch / rows
-        full = (t1 - t0) + scale_rows * ((t3 - t2) * self.num_layers / layers + (t4 - t3))
-        return {"planner_s": t1 - t0, "layers_s": t3 - t2, "head_sampler_s": t4 - t3, "full_step_s": full,
-                "rows": rows, "layers": layers}
+        return {"planner_s": t1 - t0, "layers_s": t2 - t1, "head_sampler_s": t3 - t2, "step_s": t3 - t0,
+                "layers": layers}

@@ -125,3 +125,76 @@ def test_binding_rejects_oversized_metadata(nqt, cuda):
         b.plan(m)
     with pytest.raises(IndexError):
         b.select_layer(1)
+
+
+def _empty_meta(nqt, rows, prefill):
+    return nqt.TalkerAttentionMetadata(
+        qo_indptr=torch.zeros(rows + 1, dtype=torch.int32) if prefill else None,
+        paged_kv_indptr=torch.arange(rows + 1, dtype=torch.int32),
+        paged_kv_indices=torch.arange(rows, dtype=torch.int32),
+        paged_kv_last_page_len=torch.ones(rows, dtype=torch.int32),
+        position_ids=torch.zeros(rows, dtype=torch.long), write_pages=torch.arange(rows, dtype=torch.long),
+        write_offsets=torch.zeros(rows, dtype=torch.long), padding_pages=())
+
+
+def test_binding_kind_is_fixed_by_its_first_plan(nqt, cuda):
+    """The reference decode binding rejects packed query metadata and the
+    prefill binding requires it (executor/talker_kv.py:176-177, 260-261)."""
+
+    storage = torch.zeros(1, 8, 2, 16, 8, 128, dtype=torch.bfloat16, device=cuda)
+    dec = _binding(nqt, cuda, storage, 2, 2)
+    dec.plan(_empty_meta(nqt, 2, False))
+    with pytest.raises(ValueError, match="Talker decode cannot contain packed query metadata"):
+        dec.plan(_empty_meta(nqt, 2, True))
+    pre = _binding(nqt, cuda, storage, 2, 2)
+    pre.plan(_empty_meta(nqt, 2, True))
+    with pytest.raises(ValueError, match="Talker prefill requires packed query metadata"):
+        pre.plan(_empty_meta(nqt, 2, False))
+    fixed = nqt.B200TalkerBinding(storage=storage, capture_batch_size=2, token_capacity=2, num_qo_heads=16,
+                                  num_kv_heads=8, head_dim=128, page_size=16, total_pages=8, device=cuda,
+                                  dtype=torch.bfloat16, mode="prefill")
+    with pytest.raises(ValueError, match="Talker prefill requires packed query metadata"):
+        fixed.plan(_empty_meta(nqt, 2, False))
+
+
+def test_bindings_share_the_slot_workspace(nqt, cuda):
+    """Two decode bindings of one slot keep their split-KV plans in the slot's
+    workspace (like the reference's per-slot FlashInfer workspace); planning
+    before each run keeps both correct."""
+
+    g = torch.Generator().manual_seed(5)
+    pages, P = 96, 16
+    storage_cpu = torch.randn(1, pages, 2, P, 8, 128, generator=g).to(torch.bfloat16)
+    storage = storage_cpu.to(cuda)
+    attn = FakeAttention(torch.ones(128, dtype=torch.bfloat16, device=cuda),
+                         torch.ones(128, dtype=torch.bfloat16, device=cuda))
+    workspace = torch.empty(64 << 20, dtype=torch.uint8, device=cuda)
+
+    def make(rows):
+        return nqt.binding_factory(storage=storage, capture_batch_size=rows, token_capacity=rows, num_qo_heads=16,
+                                   num_kv_heads=8, head_dim=128, page_size=P, total_pages=pages, workspace=workspace,
+                                   shared_plan_state=None, device=cuda, dtype=torch.bfloat16, slot=0, metadata=None)
+
+    a, b = make(2), make(3)
+    assert a.decode_workspace.data_ptr() == workspace.data_ptr() == b.decode_workspace.data_ptr()
+    pool = oplan.HostPagePool(pages, P, 3)
+    for r, n in (("x", 700), ("y", 33), ("z", 400)):
+        pool.add_request(r)
+        pool.reserve([r], [n])
+        pool.publish(r)
+    cases = ((a, ["x", "y"], 2), (b, ["x", "y", "z"], 3), (a, ["y", "z"], 2))
+    for binding, rids, rows in cases:
+        m = pool.metadata(rids, [1] * rows, rows, rows, False)
+        binding.plan(_meta(nqt, m, False))
+        binding.select_layer(0)
+        qkv = torch.randn(rows, 32 * 128, generator=g).to(torch.bfloat16)
+        q, k, v = qkv[:, :2048].view(rows, 16, 128), qkv[:, 2048:3072].view(rows, 8, 128), qkv[:, 3072:].view(rows, 8, 128)
+        want = _oracle_attend(storage_cpu[0], m, q, k, v, attn, False)
+        qd = qkv.to(cuda)
+        got = binding.attend(attn, qd[:, :2048].view(rows, 16, 128), qd[:, 2048:3072].view(rows, 8, 128),
+                             qd[:, 3072:].view(rows, 8, 128))
+        torch.testing.assert_close(got.float().cpu(), want, atol=2e-2, rtol=0)
+        for r in rids:
+            pool.discard(r)
+        storage_cpu.copy_(storage.cpu())
+    assert nqt.kernels.read_status(cuda) == 0

@@ -50,8 +50,9 @@ def test_noalloc_decode_matches_workspace_decode_twice(nqt, cuda):
         got = torch.full_like(want, float("nan"))
         _noalloc(lib_mod, q, cache, indptr, indices, last, got, status)
         torch.cuda.synchronize()
-        # same kernels, same split: agreement well inside the 2e-2 attention tolerance
-        torch.testing.assert_close(got.float(), want.float(), atol=2e-2, rtol=0)
+        # same kernels and the same split (both cap the split CTAs above the 2-per-SM grid), and the split
+        # partials are combined in a fixed order: the outputs are identical, well inside the 2e-2 tolerance
+        assert torch.equal(got, want)
         assert int(status.item()) == 0
     assert nqt.lib().nqt_decode_noalloc_scratch_bytes() < 8 * 1024 * 1024
 
