@@ -19,30 +19,18 @@
 //      argmax(p / Exp(1)) on the CPU, so the same noise gives the same id.
 //   7. Optionally mark the sampled token in the seen mask.
 //
-// Work split: a group of G = 1, 2, 4 or 8 warps takes a row (the host picks
-// G so that rows x G fill the GPU); the group streams its row two or three
-// times (after the first pass it is an L1 hit) and its warps meet only at a
-// named barrier:
-//   histogram  256 bins of t = max(0, (m - x) / w + 64), with m and the width
-//           w = (m - mean) / 48 from a strided sample of the row.  y never
-//           decreases as x grows and t never increases, so the bins up to the
-//           one holding the k-th value hold the whole y-top-k, except for an
-//           exact tie in y made by the rounding of the quotient (checked
-//           below).  When that bin alone holds too many, its 256 sub-bins are
-//           counted in a second pass (t - bin is exact, so the split stays
-//           monotone).
-//   compaction  warp ballots collect the <= 64 candidates; y is computed for
-//           them only, they are bitonic-sorted in one warp's registers, and
-//           the largest logit left out must not tie the k-th value after the
-//           division.
-// Rows the group path cannot settle (k > 64, NaN or +inf logits, a row that
-// does not narrow to 64 candidates, a rounding tie) are marked, and after the
-// group phase the whole CTA takes each of them through the exact general path:
-// a 4-pass radix select (8 bits per pass) of the k-th key, compaction of every
-// key >= it and a bitonic sort in shared memory.
+// Work split: a group of G = 1, 2, 4 or 8 warps takes a row (the host picks G so that rows x G fill
+// the GPU and the row fits the group's lanes).  The fast path (fast_row, below) reads the row once,
+// cuts it to a few hundred candidates with a count-guaranteed threshold, takes the exact penalty and
+// division only for those, and ranks at most 128 of them in one warp.  Rows it cannot settle (k > 64,
+// a penalty below 1 with a seen mask, NaN or +inf logits, unaligned or oversized rows, a candidate
+// capacity overflow, or a rounding tie at the k-th value) are marked, and after the fast phase the
+// whole CTA takes each of them through the exact general path: a 4-pass radix select (8 bits per
+// pass) of the k-th key, compaction of every key >= it and a bitonic sort in shared memory.
 //
 // Reference semantics: sample_logits_stateless / _cpu_sample_row
 // (model/sampling.py:55-95, 127-225).
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -53,10 +41,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;  // rows per CTA
 constexpr int kMaxVocab = 16384;
-constexpr int kFastK = 64;        // largest top-k of the warp path
-constexpr int kBins = 256;        // histogram bins of the warp path
-constexpr float kGapBins = 48.f;    // bin width = (sample max - sample mean) / kGapBins
-constexpr float kBinsAbove = 64.f;  // bins kept for the logits above the sample's max
+constexpr int kFastK = 64;        // largest top-k of the fast path
 constexpr float kFltMax = 3.402823466e38f;
 
 struct SampleArgs {
@@ -97,13 +82,25 @@ __device__ __forceinline__ uint4 philox4x32_10(uint4 ctr, uint2 key) {
   return ctr;
 }
 
-__device__ __forceinline__ float exp_noise(int64_t seed, int64_t offset, int rank) {
-  const uint4 ctr = make_uint4(static_cast<uint32_t>(rank), 0u, static_cast<uint32_t>(offset),
+// Exp(1) noise of draw rank r: one Philox4x32-10 block keyed by the row's seed, with counter
+// (r / 128 * 32 + r % 32, 0, offset) and output word (r / 32) % 4, so one block serves ranks l, l + 32,
+// l + 64 and l + 96 (a warp's lane l draws ranks l and l + 32 from one block).
+__device__ __forceinline__ uint4 noise_block(int64_t seed, int64_t offset, int counter) {
+  const uint4 ctr = make_uint4(static_cast<uint32_t>(counter), 0u, static_cast<uint32_t>(offset),
                                static_cast<uint32_t>(static_cast<uint64_t>(offset) >> 32));
   const uint2 key = make_uint2(static_cast<uint32_t>(seed), static_cast<uint32_t>(static_cast<uint64_t>(seed) >> 32));
-  const uint4 r = philox4x32_10(ctr, key);
-  const float u = (static_cast<float>(r.x >> 8) + 0.5f) * 5.9604644775390625e-8f;  // (0, 1)
+  return philox4x32_10(ctr, key);
+}
+
+__device__ __forceinline__ float exp_of_word(uint32_t w) {
+  const float u = (static_cast<float>(w >> 8) + 0.5f) * 5.9604644775390625e-8f;  // (0, 1)
   return -logf(u);
+}
+
+__device__ __forceinline__ float exp_noise(int64_t seed, int64_t offset, int rank) {
+  const uint4 r = noise_block(seed, offset, (rank >> 7) * 32 + (rank & 31));
+  const int word = (rank >> 5) & 3;
+  return exp_of_word(word == 0 ? r.x : (word == 1 ? r.y : (word == 2 ? r.z : r.w)));
 }
 
 __device__ __forceinline__ uint32_t order_key(float v) {
@@ -196,32 +193,29 @@ __device__ __forceinline__ int warp_incl_scan(int v) {
   return v;
 }
 
-// Bitonic sort (descending) of 64 keys held two per lane: rank i lives in
-// lane i % 32, slot i / 32.  Pairs closer than 32 ranks are exchanged with
-// shuffles; the j == 32 step is a swap between a lane's two slots.
+// Bitonic sort (descending) of 64 keys held two per lane (rank i in lane i % 32, slot i / 32), in the
+// flip form of warp_sort64_desc_f32 (one lower-lane predicate per step).
 __device__ __forceinline__ void warp_sort64_desc(uint64_t& v0, uint64_t& v1) {
   const int lane = threadIdx.x & 31;
+  auto cmp = [&](int dist, int bit) {
+    const uint64_t p0 = __shfl_xor_sync(kFull, v0, dist);
+    const uint64_t p1 = __shfl_xor_sync(kFull, v1, dist);
+    const bool lower = (lane & bit) == 0;
+    v0 = (lower == (p0 > v0)) ? p0 : v0;
+    v1 = (lower == (p1 > v1)) ? p1 : v1;
+  };
 #pragma unroll
-  for (int k = 2; k <= 64; k <<= 1) {
+  for (int k = 2; k <= 32; k <<= 1) {
+    cmp(k - 1, k >> 1);
 #pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      if (j == 32) {
-        if (v0 < v1) {
-          const uint64_t t = v0;
-          v0 = v1;
-          v1 = t;
-        }
-      } else {
-        const uint64_t p0 = __shfl_xor_sync(kFull, v0, j);
-        const uint64_t p1 = __shfl_xor_sync(kFull, v1, j);
-        const bool lower = (lane & j) == 0;
-        const bool max0 = lower == ((lane & k) == 0);
-        const bool max1 = lower == (((lane + 32) & k) == 0);
-        v0 = max0 ? (v0 > p0 ? v0 : p0) : (v0 < p0 ? v0 : p0);
-        v1 = max1 ? (v1 > p1 ? v1 : p1) : (v1 < p1 ? v1 : p1);
-      }
-    }
+    for (int j = k >> 2; j > 0; j >>= 1) cmp(j, j);
   }
+  const uint64_t r0 = __shfl_sync(kFull, v1, 31 - lane);
+  const uint64_t r1 = __shfl_sync(kFull, v0, 31 - lane);
+  v0 = v0 > r0 ? v0 : r0;
+  v1 = v1 < r1 ? v1 : r1;
+#pragma unroll
+  for (int j = 16; j > 0; j >>= 1) cmp(j, j);
 }
 
 struct RowParams {
@@ -252,179 +246,6 @@ template <typename T>
 __device__ __forceinline__ float scaled(const SampleArgs& a, const RowParams& p, float x) {
   const float y = __fdiv_rn(x, p.temp);
   return a.round_scaled ? to_f32(from_f32<T>(y)) : y;
-}
-
-// ---- the group path ---------------------------------------------------------
-// G warps (1, 2, 4 or 8) take one row together; the host picks G so that the
-// rows times G fill the GPU.  Every decision that needs the whole row is made
-// by each warp of the group from the same shared data, so the warps only meet
-// at the group barrier.
-
-template <int G>
-struct GroupShared {
-  int hist[kBins];
-  uint64_t slots[G][kFastK];
-  float x_out[G];
-  int count[G];
-  float best_v[G];
-  int best_i[G];
-};
-
-// Named barrier 1 + group over the group's G * 32 threads (immediate
-// operands, so the CTA reserves only the barriers it uses).
-template <int G>
-__device__ __forceinline__ void group_sync(int group) {
-  if constexpr (G == 1) {
-    __syncwarp();
-  } else if constexpr (G == 8) {
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-  } else if constexpr (G == 4) {
-    if (group == 0) {
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-    } else {
-      asm volatile("bar.sync 2, 128;" ::: "memory");
-    }
-  } else {
-    static_assert(G == 2, "groups of 1, 2, 4 or 8 warps");
-    switch (group) {
-      case 0: asm volatile("bar.sync 1, 64;" ::: "memory"); break;
-      case 1: asm volatile("bar.sync 2, 64;" ::: "memory"); break;
-      case 2: asm volatile("bar.sync 3, 64;" ::: "memory"); break;
-      default: asm volatile("bar.sync 4, 64;" ::: "memory"); break;
-    }
-  }
-}
-
-// The group's view of its row: every pass streams the row again (16-byte
-// vectors when aligned, else elements); after the first pass the row is an
-// L1 hit.  for_each calls f(e, x, valid) with x penalised; every lane of a
-// warp makes the same number of calls, so f may use warp collectives.
-template <typename T, int G, bool SEEN>
-struct GroupRow {
-  static constexpr int kVec = 16 / static_cast<int>(sizeof(T));
-  using SeenBits = typename std::conditional<kVec == 8, uint64_t, uint32_t>::type;
-  const T* lrow;
-  const uint8_t* srow;
-  int V;
-  float pen;
-  int gl;  // lane index within the group, 0 .. G * 32 - 1
-  bool vec;
-
-  __device__ __forceinline__ GroupRow(const T* l, const uint8_t* s, int vocab, float p, int group_lane)
-      : lrow(l), srow(s), V(vocab), pen(p), gl(group_lane) {
-    vec = (reinterpret_cast<uintptr_t>(lrow) & 15u) == 0 && V % kVec == 0 &&
-          (!SEEN || (reinterpret_cast<uintptr_t>(srow) % kVec) == 0);
-  }
-
-  __device__ __forceinline__ float pen_of(float x, bool seen) const {
-    if constexpr (SEEN) return penalised(x, seen, pen);
-    return x;
-  }
-
-  template <class F>
-  __device__ __forceinline__ void for_each(F&& f) const {
-    if (vec) {
-      const int chunks = V / kVec;
-      constexpr int kUnroll = sizeof(T) == 4 ? 4 : 2;
-      constexpr int kStride = G * 32;
-      for (int c0 = 0; c0 < chunks; c0 += kStride * kUnroll) {
-        uint4 r[kUnroll];
-        SeenBits b[kUnroll];
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          const int c = c0 + u * kStride + gl;
-          r[u] = c < chunks ? reinterpret_cast<const uint4*>(lrow)[c] : make_uint4(0u, 0u, 0u, 0u);
-          b[u] = 0;
-          if constexpr (SEEN) b[u] = c < chunks ? reinterpret_cast<const SeenBits*>(srow)[c] : SeenBits(0);
-        }
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          const int c = c0 + u * kStride + gl;
-          const T* t = reinterpret_cast<const T*>(&r[u]);
-#pragma unroll
-          for (int q = 0; q < kVec; ++q) {
-            f(c * kVec + q, pen_of(to_f32(t[q]), ((b[u] >> (8 * q)) & 0xffu) != 0), c < chunks);
-          }
-        }
-      }
-    } else {
-      for (int base = 0; base < V; base += G * 32) {
-        const int e = base + gl;
-        const bool valid = e < V;
-        float x = 0.f;
-        if (valid) x = pen_of(to_f32(lrow[e]), SEEN && srow[e] != 0);
-        f(e, x, valid);
-      }
-    }
-  }
-
-  // One strided sample of the row, the same in every warp (one vector or a
-  // few elements per lane, spread over the row), for the histogram's bin
-  // width: max, sum and count of the finite values.
-  __device__ __forceinline__ void sample(float& m, float& sum, int& n) const {
-    const int lane = threadIdx.x & 31;
-    m = -__builtin_huge_valf();
-    sum = 0.f;
-    n = 0;
-    auto add = [&](float x) {
-      const bool fin = x >= -kFltMax && x <= kFltMax;
-      m = fin ? fmaxf(m, x) : m;
-      sum += fin ? x : 0.f;
-      n += fin ? 1 : 0;
-    };
-    if (vec) {
-      const int chunks = V / kVec;
-      const int c = static_cast<int>((static_cast<int64_t>(lane) * chunks) >> 5);
-      const uint4 r = reinterpret_cast<const uint4*>(lrow)[c];
-      const T* t = reinterpret_cast<const T*>(&r);
-#pragma unroll
-      for (int q = 0; q < kVec; ++q) {
-        bool seen = false;
-        if constexpr (SEEN) seen = srow[c * kVec + q] != 0;
-        add(pen_of(to_f32(t[q]), seen));
-      }
-    } else {
-      for (int j = 0; j < kVec; ++j) {
-        const int e = static_cast<int>((static_cast<int64_t>(lane * kVec + j) * V) / (32 * kVec));
-        add(pen_of(to_f32(lrow[e]), SEEN && srow[e] != 0));
-      }
-    }
-    m = warp_max(m);
-    sum = warp_sum(sum);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(kFull, n, o);
-  }
-};
-
-// Bins of one histogram: lane owns bins 8 * lane .. 8 * lane + 7.  Returns
-// the first bin whose count, added to `base`, reaches k (-1 if none) and the
-// counts before it and through it.
-__device__ __forceinline__ int warp_pick_bin(const int* hist, int k, int base, int& above, int& total) {
-  const int lane = threadIdx.x & 31;
-  int c[8];
-  int mine = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    c[i] = hist[8 * lane + i];
-    mine += c[i];
-  }
-  int run = warp_incl_scan(mine) - mine + base;
-  int found = -1, f_above = 0, f_total = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (found < 0 && run + c[i] >= k) {
-      found = 8 * lane + i;
-      f_above = run;
-      f_total = run + c[i];
-    }
-    run += c[i];
-  }
-  const unsigned bal = __ballot_sync(kFull, found >= 0);
-  if (bal == 0u) return -1;
-  const int src = __ffs(bal) - 1;
-  above = __shfl_sync(kFull, f_above, src);
-  total = __shfl_sync(kFull, f_total, src);
-  return __shfl_sync(kFull, found, src);
 }
 
 // Softmax, top-p and the draw over <= 64 ranked candidates in one warp:
@@ -490,168 +311,492 @@ __device__ __forceinline__ void finish_row(const SampleArgs& a, int row, int tok
   if (a.update_seen && a.seen != nullptr) a.seen[row * a.seen_stride + token] = 1;
 }
 
-// One row in a group of G warps (warp wg of the group).  Returns false when
-// the row needs the general path; only the group's warp 0 reports that.
-template <typename T, int G, bool SEEN>
-__device__ bool group_row(const SampleArgs& a, const RowParams& p, int row, int group, int wg, GroupShared<G>& gs) {
-  const int V = a.vocab, lane = threadIdx.x & 31;
-  const T* lrow = static_cast<const T*>(a.logits) + row * a.lstride;
-  const uint8_t* srow = SEEN ? a.seen + row * a.seen_stride : nullptr;
-  const int64_t pbase = static_cast<int64_t>(row) * V;
-  const GroupRow<T, G, SEEN> src(lrow, srow, V, p.pen, wg * 32 + lane);
+// ---- the fast path ----------------------------------------------------------
+// A group of G warps (1, 2, 4 or 8) takes one row; its lanes hold the whole row in registers as
+// 16-byte vectors (vector c in group lane c % (32 G), slot c / (32 G)), so the row crosses HBM once
+// and every later pass runs on registers or on a few hundred candidates in shared memory.
+//
+//   cut 1   The row is split into 64 chunks (by lane and slot).  tau0 = the k-th largest chunk
+//           maximum: the k chunks whose maxima reach tau0 hold at least k elements >= tau0, so the
+//           raw top-k lies in C = {x >= tau0}.  A repetition penalty >= 1 only lowers a logit, so C
+//           also holds the top-k of the penalised row whenever the check below passes.  The maxima
+//           come from packed (x2) NaN-propagating max instructions on the raw vectors.
+//   prefilter  A vector whose packed maximum is below tau0 holds no candidate; the others (about
+//           a quarter) are copied to shared memory, then expanded element by element with warp
+//           ballots into C (at most 256).
+//   exact   Only the candidates read their seen-mask byte and take the exact penalty; when C has
+//           more than 64, tau1 = the k-th largest of the 64 lane-local top-2 values narrows it to
+//           F = {x_pen >= tau1} (at least k), else F = C.  y = x_pen / T for F only; F is sorted in
+//           one warp's registers (value desc, token id asc).
+//   check   Every element outside F has x_pen <= x_out = max(largest penalised candidate left out,
+//           largest input value below tau0).  If y(x_out) does not stay strictly below the k-th
+//           value, or any capacity above overflows, the row goes to the exact general path.
+// Greedy rows are the k = 1 case with y = x_pen.
+constexpr int kChunks = 64;    // chunk maxima behind cut 1
+constexpr int kCvCap = 160;    // candidate vectors per row
+constexpr int kCandCap = 256;  // candidate elements per row
 
-  if (!(p.temp > 0.f)) {
-    // greedy: first argmax of the penalised logits
-    float bv = -__builtin_huge_valf();
-    int bi = 0x7fffffff;
-    src.for_each([&](int e, float x, bool valid) {
-      if (valid) argmax_merge(bv, bi, x, e);
-    });
-    warp_argmax(bv, bi);
-    if (lane == 0) {
-      gs.best_v[wg] = bv;
-      gs.best_i[wg] = bi;
-    }
-    group_sync<G>(group);
-    bv = gs.best_v[0];
-    bi = gs.best_i[0];
-#pragma unroll
-    for (int w = 1; w < G; ++w) argmax_merge(bv, bi, gs.best_v[w], gs.best_i[w]);
-    const int token = bi < V ? bi : 0;
-    if (a.probs != nullptr) {
-      for (int r = wg * 32 + lane; r < V; r += G * 32) {
-        a.probs[pbase + r] = r == 0 ? 1.f : 0.f;
-        a.ids[pbase + r] = r == 0 ? token : -1;
-      }
-    }
-    if (wg == 0 && lane == 0) finish_row(a, row, token);
-    return true;
+// Vectors per lane of the register-resident row, per group size (V <= 32 G kVpl * elements/vector).
+template <int G>
+struct Vpl {
+  static constexpr int value = G == 1 ? 12 : (G == 2 ? 8 : 4);
+};
+
+// Packed-vector helpers per element type: a 16-byte vector is 8 bf16 / 8 fp16 / 4 fp32.
+template <typename T>
+struct Lanes;
+
+__device__ __forceinline__ uint32_t u32_of(__nv_bfloat162 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ uint32_t u32_of(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __nv_bfloat162 bf2_of(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+__device__ __forceinline__ __half2 h2_of(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+__device__ __forceinline__ float max_nan_f32(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+template <>
+struct Lanes<__nv_bfloat16> {
+  static constexpr int kVec = 8;
+  static constexpr uint32_t kNegInf = 0xFF80FF80u;
+  // two partial maxima (NaN-propagating) of the vector's 8 elements
+  static __device__ __forceinline__ uint32_t vmax(const uint4& v) {
+    return u32_of(__hmax2_nan(__hmax2_nan(bf2_of(v.x), bf2_of(v.y)), __hmax2_nan(bf2_of(v.z), bf2_of(v.w))));
   }
-  const int k_eff = p.k_eff;
-  if (k_eff > kFastK) return false;
+  static __device__ __forceinline__ uint32_t pmax(uint32_t a, uint32_t b) {
+    return u32_of(__hmax2_nan(bf2_of(a), bf2_of(b)));
+  }
+  static __device__ __forceinline__ float fold(uint32_t m) {
+    const __nv_bfloat162 h = bf2_of(m);
+    return __bfloat162float(__hmax_nan(h.x, h.y));
+  }
+  static __device__ __forceinline__ uint32_t splat(float t) { return u32_of(__float2bfloat162_rn(t)); }
+  static __device__ __forceinline__ bool any_ge(uint32_t m, uint32_t t2) {
+    return __hge2_mask(bf2_of(m), bf2_of(t2)) != 0u;
+  }
+  static __device__ __forceinline__ uint32_t any_ge_mask(uint32_t m, uint32_t t2) {
+    return __hge2_mask(bf2_of(m), bf2_of(t2));
+  }
+  static __device__ __forceinline__ float elem(const uint4& v, int e) {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(&v)[e]);
+  }
+  // element e (a runtime index) without indexing into a local array
+  static __device__ __forceinline__ float elem_dyn(const uint4& v, int e) {
+    const uint32_t w = (e & 4) ? ((e & 2) ? v.w : v.z) : ((e & 2) ? v.y : v.x);
+    return __uint_as_float((e & 1) ? (w & 0xFFFF0000u) : (w << 16));
+  }
+  // largest bf16 value below t (t a finite bf16 value)
+  static __device__ __forceinline__ float prev(float t) {
+    if (t == 0.f) return -__bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(1)));
+    const unsigned short b = __bfloat16_as_ushort(__float2bfloat16_rn(t));
+    return __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(t > 0.f ? b - 1 : b + 1)));
+  }
+};
 
-  // the draw's noise for ranks lane and lane + 32 (the group's warp 0 draws)
+template <>
+struct Lanes<__half> {
+  static constexpr int kVec = 8;
+  static constexpr uint32_t kNegInf = 0xFC00FC00u;
+  static __device__ __forceinline__ uint32_t vmax(const uint4& v) {
+    return u32_of(__hmax2_nan(__hmax2_nan(h2_of(v.x), h2_of(v.y)), __hmax2_nan(h2_of(v.z), h2_of(v.w))));
+  }
+  static __device__ __forceinline__ uint32_t pmax(uint32_t a, uint32_t b) { return u32_of(__hmax2_nan(h2_of(a), h2_of(b))); }
+  static __device__ __forceinline__ float fold(uint32_t m) {
+    const __half2 h = h2_of(m);
+    return __half2float(__hmax_nan(h.x, h.y));
+  }
+  static __device__ __forceinline__ uint32_t splat(float t) { return u32_of(__float2half2_rn(t)); }
+  static __device__ __forceinline__ bool any_ge(uint32_t m, uint32_t t2) { return __hge2_mask(h2_of(m), h2_of(t2)) != 0u; }
+  static __device__ __forceinline__ uint32_t any_ge_mask(uint32_t m, uint32_t t2) { return __hge2_mask(h2_of(m), h2_of(t2)); }
+  static __device__ __forceinline__ float elem(const uint4& v, int e) {
+    return __half2float(reinterpret_cast<const __half*>(&v)[e]);
+  }
+  static __device__ __forceinline__ float elem_dyn(const uint4& v, int e) {
+    const uint32_t w = (e & 4) ? ((e & 2) ? v.w : v.z) : ((e & 2) ? v.y : v.x);
+    return __half2float(__ushort_as_half(static_cast<unsigned short>((e & 1) ? (w >> 16) : (w & 0xFFFFu))));
+  }
+  static __device__ __forceinline__ float prev(float t) {
+    if (t == 0.f) return -__half2float(__ushort_as_half(static_cast<unsigned short>(1)));
+    const unsigned short b = __half_as_ushort(__float2half_rn(t));
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(t > 0.f ? b - 1 : b + 1)));
+  }
+};
+
+template <>
+struct Lanes<float> {
+  static constexpr int kVec = 4;
+  static constexpr uint32_t kNegInf = 0xFF800000u;
+  static __device__ __forceinline__ uint32_t vmax(const uint4& v) {
+    return __float_as_uint(max_nan_f32(max_nan_f32(__uint_as_float(v.x), __uint_as_float(v.y)),
+                                       max_nan_f32(__uint_as_float(v.z), __uint_as_float(v.w))));
+  }
+  static __device__ __forceinline__ uint32_t pmax(uint32_t a, uint32_t b) {
+    return __float_as_uint(max_nan_f32(__uint_as_float(a), __uint_as_float(b)));
+  }
+  static __device__ __forceinline__ float fold(uint32_t m) { return __uint_as_float(m); }
+  static __device__ __forceinline__ uint32_t splat(float t) { return __float_as_uint(t); }
+  static __device__ __forceinline__ bool any_ge(uint32_t m, uint32_t t) { return __uint_as_float(m) >= __uint_as_float(t); }
+  static __device__ __forceinline__ float elem(const uint4& v, int e) { return reinterpret_cast<const float*>(&v)[e]; }
+  static __device__ __forceinline__ float elem_dyn(const uint4& v, int e) {
+    return __uint_as_float((e & 2) ? ((e & 1) ? v.w : v.z) : ((e & 1) ? v.y : v.x));
+  }
+  static __device__ __forceinline__ float prev(float t) {
+    if (t == 0.f) return -__uint_as_float(1u);
+    const uint32_t b = __float_as_uint(t);
+    return __uint_as_float(t > 0.f ? b - 1u : b + 1u);
+  }
+};
+
+template <int G>
+struct FastShared {
+  uint4 cv[kCvCap];     // candidate vectors
+  int cvi[kCvCap];      // their vector index in the row
+  float cx[kCandCap];   // candidate values (raw)
+  int cid[kCandCap];    // candidate token ids
+  float fx[2 * kFastK];  // the narrowed set F: penalised values
+  int fid[2 * kFastK];   // and token ids
+  float cm[kChunks];    // chunk maxima (groups of more than one warp)
+  int wsum[G];          // candidate vectors per warp
+  float tau0;
+  int bad;
+};
+
+// Named barrier 1 + group over the group's G * 32 threads (immediate operands, so the CTA reserves only
+// the barriers it uses); a single warp only needs __syncwarp.
+template <int G>
+__device__ __forceinline__ void group_sync(int group) {
+  if constexpr (G == 1) {
+    __syncwarp();
+  } else if constexpr (G == 8) {
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+  } else if constexpr (G == 4) {
+    if (group == 0) {
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    } else {
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+    }
+  } else {
+    static_assert(G == 2, "groups of 1, 2, 4 or 8 warps");
+    switch (group) {
+      case 0: asm volatile("bar.sync 1, 64;" ::: "memory"); break;
+      case 1: asm volatile("bar.sync 2, 64;" ::: "memory"); break;
+      case 2: asm volatile("bar.sync 3, 64;" ::: "memory"); break;
+      default: asm volatile("bar.sync 4, 64;" ::: "memory"); break;
+    }
+  }
+}
+
+// Bitonic sort (descending) of 64 floats held two per lane (rank i in lane i % 32, slot i / 32), in the
+// form where every comparator keeps the larger value at the lower index: stage k opens with a flip
+// comparator between i and i ^ (k - 1) inside each k-block, then half-cleaners at distances k/4 .. 1,
+// so one predicate per step (the pair's lower lane) serves both slots.  Stage 64's flip pairs rank i
+// with rank 63 - i across the slots.
+__device__ __forceinline__ void warp_sort64_desc_f32(float& v0, float& v1) {
+  const int lane = threadIdx.x & 31;
+  auto cmp = [&](int dist, int bit) {
+    const float p0 = __shfl_xor_sync(kFull, v0, dist);
+    const float p1 = __shfl_xor_sync(kFull, v1, dist);
+    const bool lower = (lane & bit) == 0;
+    v0 = lower ? fmaxf(v0, p0) : fminf(v0, p0);
+    v1 = lower ? fmaxf(v1, p1) : fminf(v1, p1);
+  };
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+    cmp(k - 1, k >> 1);
+#pragma unroll
+    for (int j = k >> 2; j > 0; j >>= 1) cmp(j, j);
+  }
+  const float r0 = __shfl_sync(kFull, v1, 31 - lane);
+  const float r1 = __shfl_sync(kFull, v0, 31 - lane);
+  v0 = fmaxf(v0, r0);
+  v1 = fminf(v1, r1);
+#pragma unroll
+  for (int j = 16; j > 0; j >>= 1) cmp(j, j);
+}
+
+// Value of rank r of a 64-entry warp sort (held two per lane).
+__device__ __forceinline__ float rank_value(float v0, float v1, int r) {
+  return __shfl_sync(kFull, r < 32 ? v0 : v1, r & 31);
+}
+
+// Top 64 of two descending 64-entry warp sorts (a, b; rank i in lane i % 32, slot i / 32), sorted into a:
+// max(a[i], b[63 - i]) is a bitonic sequence holding the 64 largest, then a descending bitonic merge.
+__device__ __forceinline__ void warp_merge64_desc(uint64_t& a0, uint64_t& a1, uint64_t b0, uint64_t b1) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t r0 = __shfl_sync(kFull, b1, 31 - lane);  // b[63 - lane]
+  const uint64_t r1 = __shfl_sync(kFull, b0, 31 - lane);  // b[31 - lane]
+  a0 = a0 > r0 ? a0 : r0;
+  a1 = a1 > r1 ? a1 : r1;
+  if (a0 < a1) {
+    const uint64_t t = a0;
+    a0 = a1;
+    a1 = t;
+  }
+#pragma unroll
+  for (int j = 16; j > 0; j >>= 1) {
+    const uint64_t p0 = __shfl_xor_sync(kFull, a0, j);
+    const uint64_t p1 = __shfl_xor_sync(kFull, a1, j);
+    const bool lower = (lane & j) == 0;
+    a0 = lower ? (a0 > p0 ? a0 : p0) : (a0 < p0 ? a0 : p0);
+    a1 = lower ? (a1 > p1 ? a1 : p1) : (a1 < p1 ? a1 : p1);
+  }
+}
+
+// Candidate elements of one 16-byte vector that reach tau: bit e set for element e.
+template <typename T>
+__device__ __forceinline__ uint32_t vec_take_mask(const uint4& v, float tau, uint32_t tau2) {
+  if constexpr (sizeof(T) == 2) {
+    using L = Lanes<T>;
+    (void)tau;
+    uint32_t bits = 0u;
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t m = L::any_ge_mask(w[q], tau2);  // 0xFFFF in each half that reaches tau
+      bits |= ((m & 1u) | ((m >> 15) & 2u)) << (2 * q);
+    }
+    return bits;
+  } else {
+    (void)tau2;
+    uint32_t bits = 0u;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) bits |= (Lanes<T>::elem(v, e) >= tau ? 1u : 0u) << e;
+    return bits;
+  }
+}
+
+// One row on the fast path, group of G warps (this is warp wg).  Returns false when the row needs the
+// general path; every warp of the group returns the same value until the group's warp 0 works alone.
+template <typename T, int G, bool SEEN>
+__device__ bool fast_row(const SampleArgs& a, RowParams p, int row, int group, int wg, FastShared<G>& fs) {
+  using L = Lanes<T>;
+  constexpr int kVpl = Vpl<G>::value;
+  constexpr int kVec = L::kVec;
+  const int V = a.vocab, lane = threadIdx.x & 31;
+  const int gl = wg * 32 + lane;  // lane within the group
+  const T* lrow = static_cast<const T*>(a.logits) + row * a.lstride;
+  const uint4* vrow = reinterpret_cast<const uint4*>(lrow);
+  const int nvec = V / kVec;
+  const bool greedy = !(p.temp > 0.f);
+  if (greedy) p.k_eff = 1;
+  // uniform per row: what the fast path cannot take
+  if (p.k_eff > kFastK || (SEEN && p.pen < 1.f) || V % kVec != 0 || nvec > G * 32 * kVpl ||
+      (reinterpret_cast<uintptr_t>(lrow) & 15u) != 0)
+    return false;
+  const int k = p.k_eff;
+
+  // ---- stream the row once: packed maxima per vector and per chunk (the vectors are not kept)
+  uint32_t vm[kVpl];
+  {
+    uint4 v[kVpl];
+#pragma unroll
+    for (int j = 0; j < kVpl; ++j) {
+      const int c = gl + j * G * 32;
+      v[j] = c < nvec ? vrow[c] : make_uint4(L::kNegInf, L::kNegInf, L::kNegInf, L::kNegInf);
+    }
+#pragma unroll
+    for (int j = 0; j < kVpl; ++j) vm[j] = L::vmax(v[j]);
+  }
+  // the draw's noise (ranks lane and lane + 32 from one Philox block) while the loads are in flight
   float n0 = 1.f, n1 = 1.f;
-  if (wg == 0) {
+  if (!greedy && wg == 0) {
     if (a.noise != nullptr) {
       n0 = lane < V ? a.noise[row * a.noise_stride + lane] : 1.f;
       n1 = lane + 32 < V ? a.noise[row * a.noise_stride + lane + 32] : 1.f;
     } else {
-      n0 = exp_noise(p.seed, p.off, lane);
-      n1 = exp_noise(p.seed, p.off, lane + 32);
+      const uint4 r = noise_block(p.seed, p.off, lane);
+      n0 = exp_of_word(r.x);
+      n1 = exp_of_word(r.y);
+    }
+  }
+  uint32_t cm_even = L::kNegInf, cm_odd = L::kNegInf;
+#pragma unroll
+  for (int j = 0; j < kVpl; ++j) {
+    if (j & 1) cm_odd = L::pmax(cm_odd, vm[j]); else cm_even = L::pmax(cm_even, vm[j]);
+  }
+  float c0, c1;  // this lane's share of the 64 chunk maxima (G == 1: two per lane)
+  if constexpr (G == 1) {
+    c0 = L::fold(cm_even);
+    c1 = L::fold(cm_odd);
+  } else {
+    float m = L::fold(L::pmax(cm_even, cm_odd));
+    constexpr int kLanesPerChunk = G / 2;  // 64 chunks over 32 G lanes
+#pragma unroll
+    for (int o = 1; o < kLanesPerChunk; o <<= 1) m = max_nan_f32(m, __shfl_xor_sync(kFull, m, o));
+    if (gl % kLanesPerChunk == 0) fs.cm[gl / kLanesPerChunk] = m;
+    group_sync<G>(group);
+    c0 = fs.cm[lane];
+    c1 = fs.cm[lane + 32];
+  }
+
+  // ---- cut 1: tau0 = k-th largest chunk maximum (every warp of the group sorts the same 64 values)
+  const bool odd = (c0 != c0) || (c1 != c1) || c0 == __builtin_huge_valf() || c1 == __builtin_huge_valf();
+  if (__any_sync(kFull, odd)) return false;  // NaN or +inf: the general path handles them
+  warp_sort64_desc_f32(c0, c1);
+  const float tau0 = rank_value(c0, c1, k - 1);
+  if (!(tau0 > -__builtin_huge_valf())) return false;
+  const uint32_t tau2 = L::splat(tau0);
+  // the candidates' seen-mask bytes come from L2 later: start pulling the row's lines in now
+  if constexpr (SEEN) {
+    if (wg == 0) {
+      const uint8_t* srow = a.seen + row * a.seen_stride;
+      for (int off = lane * 128; off < V; off += 32 * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(srow + off));
     }
   }
 
-  // bin width from a strided sample: w = (sample max - sample mean) / kGapBins
-  float m, sum;
-  int n;
-  src.sample(m, sum, n);
-  const float gap = n > 1 ? m - sum / static_cast<float>(n) : 0.f;
-  if (!(gap > 1e-30f) || !(gap <= kFltMax)) return false;
-  const float inv_w = kGapBins / gap;
+  // ---- prefilter: vectors holding an element >= tau0 are read again (L1 / L2) into shared memory
+  uint32_t take = 0u;
+#pragma unroll
+  for (int j = 0; j < kVpl; ++j) take |= (gl + j * G * 32 < nvec && L::any_ge(vm[j], tau2) ? 1u : 0u) << j;
+  const int mine = __popc(take);
+  const int incl = warp_incl_scan(mine);
+  int base = incl - mine, total = __shfl_sync(kFull, incl, 31);
+  if constexpr (G > 1) {
+    if (lane == 31) fs.wsum[wg] = incl;
+    group_sync<G>(group);
+    int before = 0, all = 0;
+#pragma unroll
+    for (int w = 0; w < G; ++w) {
+      const int t = fs.wsum[w];
+      before += w < wg ? t : 0;
+      all += t;
+    }
+    base += before;
+    total = all;
+  }
+  if (total > kCvCap) return false;
+#pragma unroll
+  for (int j = 0; j < kVpl; ++j) {
+    if (take & (1u << j)) {
+      const int c = gl + j * G * 32;
+      fs.cv[base] = vrow[c];
+      fs.cvi[base] = c;
+      ++base;
+    }
+  }
+  group_sync<G>(group);
+  if (wg != 0) return true;  // the group's warp 0 finishes the row
 
-  // bin position t = max(0, (m - x) / w + kBinsAbove), one rounding (fma) in every pass; it never
-  // increases as x grows.  The first kBinsAbove bins hold the logits above the sample's max; t >= 255
-  // (and NaN) is counted nowhere.
-  auto tpos = [&](float x) { return __fmaf_rn(m - x, inv_w, kBinsAbove); };
-  for (int i = wg * 32 + lane; i < kBins; i += G * 32) gs.hist[i] = 0;
-  group_sync<G>(group);
-  src.for_each([&](int, float x, bool valid) {
-    const float t = tpos(x);
-    if (valid && t < 255.f) atomicAdd(&gs.hist[static_cast<int>(fmaxf(t, 0.f))], 1);
-  });
-  group_sync<G>(group);
-  int above = 0, total = 0;
-  const int b1 = warp_pick_bin(gs.hist, k_eff, 0, above, total);
-  if (b1 < 0) return false;
-  float t_cut = static_cast<float>(b1 + 1);
-  if (total > kFastK) {
-    // 256 sub-bins of bin b1: t - b1 is exact (Sterbenz), so the split is monotone in x
-    const float fb1 = static_cast<float>(b1);
-    group_sync<G>(group);
-    for (int i = wg * 32 + lane; i < kBins; i += G * 32) gs.hist[i] = 0;
-    group_sync<G>(group);
-    src.for_each([&](int, float x, bool valid) {
-      const float t = tpos(x);
-      if (valid && t < 255.f) {
-        const float tc = fmaxf(t, 0.f);
-        if (tc >= fb1 && tc < t_cut) atomicAdd(&gs.hist[static_cast<int>((tc - fb1) * 256.f)], 1);
+  // ---- expand the candidate vectors into C = {x >= tau0}: per-lane counts, one scan, scatter
+  int n_cand = 0;
+  for (int i0 = 0; i0 < total; i0 += 32) {
+    const int i = i0 + lane;
+    const bool ok = i < total;
+    const uint4 cvv = ok ? fs.cv[i] : make_uint4(L::kNegInf, L::kNegInf, L::kNegInf, L::kNegInf);
+    const int e0 = ok ? fs.cvi[i] * kVec : 0;
+    uint32_t bits = vec_take_mask<T>(cvv, tau0, tau2);
+    const int cnt = __popc(bits);
+    const int inc = warp_incl_scan(cnt);
+    int pos = n_cand + inc - cnt;
+    n_cand += __shfl_sync(kFull, inc, 31);
+    while (bits) {
+      const int e = __ffs(bits) - 1;
+      bits &= bits - 1u;
+      if (pos < kCandCap) {
+        fs.cx[pos] = L::elem_dyn(cvv, e);
+        fs.cid[pos] = e0 + e;
       }
-    });
-    group_sync<G>(group);
-    int above2 = 0;
-    const int s2 = warp_pick_bin(gs.hist, k_eff, above, above2, total);
-    if (s2 < 0 || total > kFastK) return false;
-    t_cut = fb1 + static_cast<float>(s2 + 1) * (1.f / 256.f);  // exact: at most 16 significant bits
+      ++pos;
+    }
+  }
+  if (n_cand > kCandCap) return false;
+  __syncwarp();
+
+  // ---- exact penalty on the candidates (slot s of lane l is candidate l + 32 s)
+  constexpr int kSlots = kCandCap / 32;
+  const int n_slots = (n_cand + 31) >> 5;  // warp-uniform: later slots are empty everywhere
+  float cx[kSlots];
+  int cid[kSlots];
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s) {
+    cx[s] = -__builtin_huge_valf();
+    cid[s] = 0;
+    if (s < n_slots) {
+      const int i = lane + 32 * s;
+      if (i < n_cand) {
+        cx[s] = fs.cx[i];
+        cid[s] = fs.cid[i];
+      }
+    }
+  }
+  if constexpr (SEEN) {
+    uint8_t sb[kSlots];
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) {
+      sb[s] = 0;
+      if (s < n_slots && lane + 32 * s < n_cand) sb[s] = a.seen[row * a.seen_stride + cid[s]];
+    }
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) {
+      if (s < n_slots && __any_sync(kFull, sb[s] != 0)) cx[s] = penalised(cx[s], sb[s] != 0, p.pen);
+    }
   }
 
-  // ballot compaction of {t < t_cut} into the warp's slots; the largest logit left out
-  int count = 0;
-  float x_out = -__builtin_huge_valf();
-  uint64_t* slots = gs.slots[wg];
-  src.for_each([&](int e, float x, bool valid) {
-    const float t = tpos(x);
-    const bool take = valid && t < 255.f && fmaxf(t, 0.f) < t_cut;
-    const unsigned bal = __ballot_sync(kFull, take);
-    if (take) {
-      const int slot = count + __popc(bal & ((1u << lane) - 1u));
-      if (slot < kFastK) slots[slot] = (static_cast<uint64_t>(__float_as_uint(x)) << 32) | static_cast<uint32_t>(e);
+  // ---- cut 2 (more than 64 candidates): tau1 = k-th largest of the 64 lane-local top-2 values
+  float tau1 = -__builtin_huge_valf();
+  if (n_cand > kFastK) {
+    // the k-th largest of the 64 lane-local top-2 values (64 distinct candidates) is a valid floor
+    float t1 = -__builtin_huge_valf(), t2 = -__builtin_huge_valf();
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) {
+      if (s < n_slots) {
+        const float x = cx[s];  // absent slots hold -inf
+        t2 = fmaxf(t2, fminf(t1, x));
+        t1 = fmaxf(t1, x);
+      }
     }
-    count += __popc(bal);
-    x_out = fmaxf(x_out, (valid && !take) ? x : -__builtin_huge_valf());
-  });
-  x_out = warp_max(x_out);
-  if (lane == 0) {
-    gs.count[wg] = count;
-    gs.x_out[wg] = x_out;
+    warp_sort64_desc_f32(t1, t2);
+    tau1 = rank_value(t1, t2, k - 1);
   }
+  // F = {x_pen >= tau1}; x_out = the largest penalised candidate left out
+  int n_f = 0;
+  float x_out = -__builtin_huge_valf();
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s) {
+    if (s < n_slots) {
+      const bool ok = lane + 32 * s < n_cand;
+      const bool in = ok && cx[s] >= tau1;
+      if (ok && !in) x_out = fmaxf(x_out, cx[s]);
+      const unsigned bal = __ballot_sync(kFull, in);
+      const int pos = n_f + __popc(bal & ((1u << lane) - 1u));
+      if (in && pos < 2 * kFastK) {
+        fs.fx[pos] = cx[s];
+        fs.fid[pos] = cid[s];
+      }
+      n_f += __popc(bal);
+    }
+  }
+  if (n_f > 2 * kFastK || n_f < k) return false;
+  x_out = warp_max(x_out);
+  __syncwarp();
+
+  // ---- rank F by (y desc, token id asc); a second block of 64 is sorted and merged in
+  auto yval = [&](float x) { return greedy ? x : scaled<T>(a, p, x); };
+  auto word = [&](int i) { return i < n_f ? cand_word(order_key(yval(fs.fx[i])), fs.fid[i]) : 0ull; };
+  uint64_t w0 = word(lane), w1 = word(lane + 32);
+  warp_sort64_desc(w0, w1);
+  if (n_f > kFastK) {
+    uint64_t b0 = word(lane + 64), b1 = word(lane + 96);
+    warp_sort64_desc(b0, b1);
+    warp_merge64_desc(w0, w1, b0, b1);
+  }
+  // check: everything outside F stays strictly below the k-th value
+  const uint64_t kth = __shfl_sync(kFull, (k - 1) < 32 ? w0 : w1, (k - 1) & 31);
+  const float x_bound = fmaxf(x_out, L::prev(tau0));
+  if (order_key(yval(x_bound)) >= static_cast<uint32_t>(kth >> 32)) return false;
+
+  // ---- softmax, top-p and the draw over the k ranks
+  const int token = draw_top64(a, p, row, w0, w1, n0, n1);
   if (a.probs != nullptr) {
-    for (int r = k_eff + wg * 32 + lane; r < V; r += G * 32) {
+    const int64_t pbase = static_cast<int64_t>(row) * V;
+    for (int r = k + lane; r < V; r += 32) {
       a.probs[pbase + r] = 0.f;
       a.ids[pbase + r] = -1;
     }
   }
-  group_sync<G>(group);
-  if (wg != 0) return true;
-
-  // the group's warp 0: y and keys for the candidates, ranked in registers
-  int total_count = 0;
-  x_out = -__builtin_huge_valf();
-  int w0 = -1, off0 = 0, w1 = -1, off1 = 0;
-#pragma unroll
-  for (int w = 0; w < G; ++w) {
-    const int cw = gs.count[w];
-    if (w0 < 0 && lane < total_count + cw) {
-      w0 = w;
-      off0 = lane - total_count;
-    }
-    if (w1 < 0 && lane + 32 < total_count + cw) {
-      w1 = w;
-      off1 = lane + 32 - total_count;
-    }
-    total_count += cw;
-    x_out = fmaxf(x_out, gs.x_out[w]);
-  }
-  if (total_count > kFastK || total_count < k_eff) return false;  // the histogram counts rule both out
-  uint64_t c0 = 0ull, c1 = 0ull;
-  if (lane < total_count) {
-    const uint64_t sl = gs.slots[w0][off0];
-    c0 = cand_word(order_key(scaled<T>(a, p, __uint_as_float(static_cast<uint32_t>(sl >> 32)))),
-                   static_cast<int>(sl & 0xffffffffu));
-  }
-  if (lane + 32 < total_count) {
-    const uint64_t sl = gs.slots[w1][off1];
-    c1 = cand_word(order_key(scaled<T>(a, p, __uint_as_float(static_cast<uint32_t>(sl >> 32)))),
-                   static_cast<int>(sl & 0xffffffffu));
-  }
-  warp_sort64_desc(c0, c1);
-  // a logit outside the candidates whose quotient ties the k-th value needs the general path
-  // (x_out = -inf when nothing was left out; its quotient cannot tie a finite candidate)
-  const uint64_t kth = __shfl_sync(kFull, (k_eff - 1) < 32 ? c0 : c1, (k_eff - 1) & 31);
-  if (x_out > -__builtin_huge_valf() && order_key(scaled<T>(a, p, x_out)) >= static_cast<uint32_t>(kth >> 32)) {
-    return false;
-  }
-  const int token = draw_top64(a, p, row, c0, c1, n0, n1);
   if (lane == 0) finish_row(a, row, token);
   return true;
 }
@@ -674,6 +819,26 @@ __device__ void block_row(const SampleArgs& a, int row, BlockShared& sh, uint64_
   const int k_eff = p.k_eff;
   const T* lrow = static_cast<const T*>(a.logits) + row * a.lstride;
   const uint8_t* srow = a.seen != nullptr ? a.seen + row * a.seen_stride : nullptr;
+  const int64_t pbase = static_cast<int64_t>(row) * V;
+
+  if (!(p.temp > 0.f)) {
+    // greedy: first argmax of the penalised logits (model/sampling.py:183-187)
+    float bv = -__builtin_huge_valf();
+    int bi = 0x7fffffff;
+    for (int e = tid; e < V; e += kThreads)
+      argmax_merge(bv, bi, penalised(to_f32(lrow[e]), srow != nullptr && srow[e] != 0, p.pen), e);
+    const int best = block_argmax(bv, bi, sh.redf, sh.redi);
+    const int token = best < V ? best : 0;
+    if (a.probs != nullptr) {
+      for (int r = tid; r < V; r += kThreads) {
+        a.probs[pbase + r] = r == 0 ? 1.f : 0.f;
+        a.ids[pbase + r] = r == 0 ? token : -1;
+      }
+    }
+    if (tid == 0) finish_row(a, row, token);
+    __syncthreads();
+    return;
+  }
 
   for (int e = tid; e < V; e += kThreads) {
     const float x = penalised(to_f32(lrow[e]), srow != nullptr && srow[e] != 0, p.pen);
@@ -803,7 +968,6 @@ __device__ void block_row(const SampleArgs& a, int row, BlockShared& sh, uint64_
   // exponential race over ranks
   float bv = -1.f;
   int br = k_eff;
-  const int64_t pbase = static_cast<int64_t>(row) * V;
   for (int r = r0; r < r1; ++r) {
     float pr = __uint_as_float(static_cast<uint32_t>(s_cand[r] >> 32));
     if (p.top_p < 1.f) pr = __fdiv_rn(pr, norm);
@@ -825,16 +989,15 @@ __device__ void block_row(const SampleArgs& a, int row, BlockShared& sh, uint64_
   __syncthreads();  // s_cand and s_key are reused by the next row
 }
 
-// Dynamic shared memory: [np2] candidates of the general path, then one
-// region that holds the groups' histograms and slots during the group phase
-// and the keys of a row on the general path afterwards.
-__host__ __device__ constexpr size_t region_bytes(int vocab, size_t group_bytes) {
-  return static_cast<size_t>(vocab) * 4 > group_bytes ? static_cast<size_t>(vocab) * 4 : group_bytes;
+// Dynamic shared memory: one region that holds the groups' fast-path buffers during the fast phase and,
+// afterwards, the general path's [np2] candidates followed by the keys of its row.
+__host__ __device__ constexpr size_t region_bytes(int np2, int vocab, size_t group_bytes) {
+  return static_cast<size_t>(np2) * 8 + static_cast<size_t>(vocab) * 4 > group_bytes
+             ? static_cast<size_t>(np2) * 8 + static_cast<size_t>(vocab) * 4
+             : group_bytes;
 }
 
-// kWarps / G rows per CTA, G warps per row.  Four CTAs per SM (at most 64 registers per thread, no
-// spills; about 45 KB of shared memory each): the passes are bound by instruction latency, so more
-// resident warps help (16384 x 3072 rows: 234 -> 179 us against two CTAs per SM).
+// kWarps / G rows per CTA, G warps per row.
 template <typename T, int G>
 __global__ void __launch_bounds__(kThreads, 4) sample_kernel(SampleArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -842,8 +1005,9 @@ __global__ void __launch_bounds__(kThreads, 4) sample_kernel(SampleArgs a) {
   __shared__ int s_rest[kWarps];
   __shared__ int s_nrest;
   constexpr int kRows = kWarps / G;
+  uint8_t* region = smem;
   uint64_t* s_cand = reinterpret_cast<uint64_t*>(smem);
-  uint8_t* region = smem + static_cast<size_t>(a.np2) * 8;
+  uint32_t* s_key = reinterpret_cast<uint32_t*>(smem + static_cast<size_t>(a.np2) * 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int group = warp / G, wg = warp % G;
   if (threadIdx.x == 0) s_nrest = 0;
@@ -851,36 +1015,43 @@ __global__ void __launch_bounds__(kThreads, 4) sample_kernel(SampleArgs a) {
   const int row = blockIdx.x * kRows + group;
   if (row < a.rows) {
     const RowParams p = row_params(a, row);
-    GroupShared<G>& gs = reinterpret_cast<GroupShared<G>*>(region)[group];
-    const bool done = a.seen != nullptr ? group_row<T, G, true>(a, p, row, group, wg, gs)
-                                        : group_row<T, G, false>(a, p, row, group, wg, gs);
+    FastShared<G>& fs = reinterpret_cast<FastShared<G>*>(region)[group];
+    const bool done = a.seen != nullptr ? fast_row<T, G, true>(a, p, row, group, wg, fs)
+                                        : fast_row<T, G, false>(a, p, row, group, wg, fs);
     if (!done && wg == 0 && lane == 0) s_rest[atomicAdd(&s_nrest, 1)] = row;
   }
   __syncthreads();
   const int nrest = s_nrest;
-  for (int i = 0; i < nrest; ++i) block_row<T>(a, s_rest[i], bs, s_cand, reinterpret_cast<uint32_t*>(region));
+  for (int i = 0; i < nrest; ++i) block_row<T>(a, s_rest[i], bs, s_cand, s_key);
 }
 
 template <typename T, int G>
 int launch_g(SampleArgs a, cudaStream_t s) {
-  const size_t smem = static_cast<size_t>(a.np2) * 8 + region_bytes(a.vocab, sizeof(GroupShared<G>) * (kWarps / G));
-  // the static shared memory counts against the default 48 KB as well
-  if (smem > 32 * 1024) {
+  const size_t smem = region_bytes(a.np2, a.vocab, sizeof(FastShared<G>) * (kWarps / G));
+  // the static shared memory counts against the default 48 KB as well; raised once per instantiation
+  static std::once_flag once;
+  std::call_once(once, [] {
     cudaFuncSetAttribute(sample_kernel<T, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  }
+  });
   constexpr int kRows = kWarps / G;
   sample_kernel<T, G><<<(a.rows + kRows - 1) / kRows, kThreads, smem, s>>>(a);
   return check_launch("sample_rows");
 }
 
-// Warps per row: enough that rows x G reaches eight warps per SM, at most 8.
+// Warps per row: enough that rows x G reaches eight warps per SM, at most 8, and enough that the
+// row fits the group's registers (larger rows take the general path).
 template <typename T>
 int launch(SampleArgs a, cudaStream_t s) {
   const int want = (8 * num_sms() + a.rows - 1) / a.rows;
-  if (want >= 5) return launch_g<T, 8>(a, s);
-  if (want >= 3) return launch_g<T, 4>(a, s);
-  if (want >= 2) return launch_g<T, 2>(a, s);
-  return launch_g<T, 1>(a, s);
+  const int nvec = a.vocab / Lanes<T>::kVec;
+  int g = want >= 5 ? 8 : (want >= 3 ? 4 : (want >= 2 ? 2 : 1));
+  while (g < 8 && nvec > g * 32 * (g == 1 ? Vpl<1>::value : (g == 2 ? Vpl<2>::value : Vpl<4>::value))) g *= 2;
+  switch (g) {
+    case 1: return launch_g<T, 1>(a, s);
+    case 2: return launch_g<T, 2>(a, s);
+    case 4: return launch_g<T, 4>(a, s);
+    default: return launch_g<T, 8>(a, s);
+  }
 }
 
 int run(SampleArgs a, int dtype, void* stream) {
