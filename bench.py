@@ -778,7 +778,7 @@ def main() -> None:
             else "growing by one token per step (published)",
         },
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
-                "d2h_bytes_per_step": BATCH * 8},
+                "d2h_bytes_per_step": step.d2h_bytes()},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "traffic_source": "scaled_from_profile: ncu DRAM bytes of one launch "
                      "on the same contexts (2-layer capture), scaled by the tokens read",

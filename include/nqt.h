@@ -435,6 +435,48 @@ int nqt_gemm_pack_weight(const void* w, int64_t ldw, int n, int k, int interleav
 int nqt_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, void* y, int64_t ldy, const void* bias,
                   int m, int n, int k, int epilogue, int split, int32_t* status, void* stream);
 
+/*
+ * Device-side request control of a talker step (no host staging before a captured step, no per-row
+ * host read after it).  Per-request state lives in a slot table on the device; rows name their slot
+ * (row_slot[r] < 0 marks a padding row).  Distinct rows must name distinct slots.
+ *
+ * nqt_step_stage gathers each row's sampler parameters from its slot - it replaces the pinned host
+ * staging of TalkerExecutor._stage_sampling_rows (executor/talker.py:527-563, padding rows take its
+ * defaults: temperature 0, top_k 1, top_p 1, penalty 1, seed 0, offset 0) - and, when suppress_eos is
+ * given, the row's EOS-suppression flag step < eos_from (engine/input_builder.py:60-70: eos_from is
+ * INT32_MAX while EOS is suppressed indefinitely, else max(2, token_count - 1) for a terminal
+ * continuation, else 2).  slot_penalty and penalty are both given or both NULL.
+ */
+int nqt_step_stage(
+    const int32_t* row_slot, int rows, int slots,
+    const float* slot_temperature, const int32_t* slot_top_k, const float* slot_top_p,
+    const float* slot_penalty, const int64_t* slot_seed, const int64_t* slot_offset,
+    const int32_t* slot_step, const int32_t* slot_eos_from,
+    float* temperature, int32_t* top_k, float* top_p, float* penalty, int64_t* seed, int64_t* offset,
+    uint8_t* suppress_eos, int32_t* status, void* stream);
+
+/*
+ * The codec head's suppress mask, in place on logits [rows, vocab] (stride logits_stride elements):
+ * columns >= codec_vocab become -inf except eos_id, and eos_id becomes -inf on rows with
+ * suppress_eos[r] != 0 (Qwen3TTSTalkerExecutor.forward_logits, executor/talker.py:170-183, 241-243).
+ * eos_id < 0: no EOS column.  suppress_eos may be NULL (no row suppressed).
+ */
+int nqt_talker_logits_mask(void* logits, int dtype, int64_t logits_stride, int rows, int vocab, int codec_vocab,
+                           int eos_id, const uint8_t* suppress_eos, void* stream);
+
+/*
+ * The decode completion rule of SynthesisPipeline (engine/pipeline.py:583-609) on the device, which
+ * replaces its per-row host read tokens[i].item(): reached_limit = step + 1 >= max_tokens;
+ * eos = tokens[r] == eos_id on a row whose EOS is not suppressed (step < eos_from) and that has not
+ * reached the limit; terminal[r] = eos || reached_limit.  Then each live row's slot advances: step + 1
+ * and offset + offset_stride (TALKER_FRAME_OFFSET_STRIDE = 512, executor/talker.py:606).
+ * n_terminal (optional) is incremented once per terminal row.
+ */
+int nqt_step_finish(const int32_t* row_slot, int rows, int slots, const int64_t* tokens, int eos_id,
+                    int32_t* slot_step, const int32_t* slot_max_tokens, const int32_t* slot_eos_from,
+                    int64_t* slot_offset, int64_t offset_stride, uint8_t* terminal, int32_t* n_terminal,
+                    int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

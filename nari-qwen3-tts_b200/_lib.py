@@ -96,6 +96,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqt_silu_and_mul": (I, [P, L, P, L, I, I, I, P]),
     "nqt_gemm_pack_weight": (I, [P, L, I, I, I, P, P]),
     "nqt_gemm_bf16": (I, [P, L, P, P, L, P, I, I, I, I, I, P, P]),
+    "nqt_step_stage": (I, [P, I, I, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
+    "nqt_talker_logits_mask": (I, [P, I, L, I, I, I, I, P, P]),
+    "nqt_step_finish": (I, [P, I, I, P, I, P, P, P, P, L, P, P, P, P]),
 }
 
 _lock = threading.Lock()

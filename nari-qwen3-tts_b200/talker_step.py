@@ -11,16 +11,19 @@ with the layer loop of model/components.py:74-90):
         attend: QK RMSNorm + RoPE + paged K/V write, paged decode (talker_kv.py)
         O projection (cuBLAS), fused residual add + RMSNorm
         gate/up (cuBLAS), SiLU * up, down (cuBLAS), fused add + RMSNorm (next norm)
-    codec head (cuBLAS), fused sampler with the seen-mask update, commit,
-    RNG offsets += 512 (executor/talker.py:606)
+    codec head (cuBLAS), suppress mask, fused sampler with the seen-mask update,
+    device completion rule (terminal flags, step and RNG offset += 512), commit
+
+The rows' sampling parameters are gathered on the device from a per-request
+slot table (step_control.py) at the start of the step instead of being staged
+from the host (executor/talker.py:527-563), and termination is decided on the
+device (engine/pipeline.py:583-609) instead of by a host read of each token.
 
 There is no host round trip inside the step.  ``step()`` is the host-facing
 call: it copies the step's inputs from pinned host memory, replays the
 graph and returns the sampled tokens to the host.
 
 Weights are random (bf16); GEMMs are plain library calls (torch -> cuBLAS).
-The suppress-token mask of forward_logits (executor/talker.py:241-243) is
-not applied.
 """
 
 from __future__ import annotations
@@ -33,6 +36,7 @@ import torch.nn.functional as F
 from . import kernels
 from .planner import DevicePagePlanner
 from .sampling import sample_rows
+from .step_control import EOS_NEVER, DeviceStepControl, RequestSampling, eos_from
 from .talker_kv import B200TalkerBinding, batch_decode_paged, batch_prefill_paged
 
 FRAME_OFFSET_STRIDE = 512  # contract/rng.py: 16 codebooks x 32
@@ -47,6 +51,8 @@ class TalkerShape:
     head_dim: int = 128
     ffn: int = 6144
     vocab: int = 3072
+    codec_vocab: int = 2048  # the code predictor's vocabulary: talker logits past it are suppressed
+    eos_id: int = 2150       # codec EOS token (inside the suppressed range, kept live)
     rope_theta: float = 1.0e6
     eps: float = 1e-6
 
@@ -153,12 +159,9 @@ class TalkerDecodeStep:
                                          mode="decode")
         # static step buffers (graph inputs and outputs)
         self.hidden_in = torch.zeros(batch, s.hidden, dtype=bf16, device=dev)
-        self.temperature = torch.full((batch,), 0.9, device=dev)
-        self.top_k = torch.full((batch,), 50, dtype=torch.int32, device=dev)
-        self.top_p = torch.full((batch,), 0.95, device=dev)
-        self.penalty = torch.full((batch,), 1.05, device=dev)
-        self.seed = torch.arange(batch, dtype=torch.long, device=dev)
-        self.offset = torch.zeros(batch, dtype=torch.long, device=dev)
+        # request state on the device: row i serves request slot i
+        self.control = DeviceStepControl(slots=batch, rows=batch, device=dev, vocab=s.vocab,
+                                         codec_vocab=s.codec_vocab, eos_id=s.eos_id)
         self.seen = torch.zeros(batch, s.vocab, dtype=torch.bool, device=dev)
         self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
         self._x = torch.empty(batch, s.hidden, dtype=bf16, device=dev)
@@ -171,11 +174,24 @@ class TalkerDecodeStep:
         # pinned host staging for step()
         self._h_hidden = torch.empty(batch, s.hidden, dtype=bf16).pin_memory()
         self._h_tokens = torch.empty(batch, dtype=torch.long).pin_memory()
+        self._h_terminal = torch.empty(batch, dtype=torch.uint8).pin_memory()
 
     # ---------------------------------------------------------------- requests
-    def admit(self, contexts: list[int], *, scatter_seed: int = 0) -> None:
+    # the rows' staged sampling parameters (written by the step itself)
+    temperature = property(lambda self: self.control.temperature)
+    top_k = property(lambda self: self.control.top_k)
+    top_p = property(lambda self: self.control.top_p)
+    penalty = property(lambda self: self.control.penalty)
+    seed = property(lambda self: self.control.seed)
+    offset = property(lambda self: self.control.offset)
+    terminal = property(lambda self: self.control.terminal)
+
+    def admit(self, contexts: list[int], *, scatter_seed: int = 0, sampling: RequestSampling | None = None,
+              max_tokens: int = EOS_NEVER, ignore_eos: bool = False) -> None:
         """Admit len(contexts) requests whose KV already fills `contexts[i]`
-        tokens, on pages scattered by a seeded permutation of the pool."""
+        tokens, on pages scattered by a seeded permutation of the pool.  Every
+        request gets ``sampling`` (default T 0.9, top-k 50, top-p 0.95,
+        penalty 1.05, seed = row, offset 0) and the completion limits."""
 
         if len(contexts) != self.batch:
             raise ValueError("admit one context per batch row")
@@ -193,6 +209,10 @@ class TalkerDecodeStep:
             slots.append(slot)
         self.planner.set_rows(slots, [1] * self.batch)
         self.contexts = list(contexts)
+        for i in range(self.batch):
+            req = sampling or RequestSampling(temperature=0.9, top_k=50, top_p=0.95, repetition_penalty=1.05, seed=i)
+            self.control.set_request(i, req, max_tokens=max_tokens, eos_from_step=eos_from(ignore_eos=ignore_eos))
+        self.control.set_rows(list(range(self.batch)))
         # repetition-penalty history: 64 recent ids per row
         ids = torch.randint(0, self.shape.vocab, (self.batch, 64), generator=g)
         self.seen.zero_()
@@ -206,6 +226,8 @@ class TalkerDecodeStep:
 
         s = self.shape
         b = self.binding
+        ctl = self.control
+        ctl.stage()
         self.planner.plan(b, prefill=False)
         x, residual = self._x, self._residual
         w = self.weights
@@ -226,14 +248,14 @@ class TalkerDecodeStep:
             x = _mlp_block(w, s, layer, o, residual, self._act)
             if trace is not None:
                 trace.append((x.clone(), residual.clone()))
-        logits = F.linear(x, w.w_head)
+        logits = ctl.mask_logits(F.linear(x, w.w_head))
         if trace is not None:
             trace.append(logits.clone())
-        sample_rows(logits, self.temperature, self.top_k, self.top_p, self.seed, self.offset,
-                    repetition_penalty=self.penalty, seen_token_mask=self.seen, update_seen=True,
+        sample_rows(logits, ctl.temperature, ctl.top_k, ctl.top_p, ctl.seed, ctl.offset,
+                    repetition_penalty=ctl.penalty, seen_token_mask=self.seen, update_seen=True,
                     round_scaled_to_input=False, noise=self.sample_noise, out=self.tokens)
+        ctl.finish(self.tokens, offset_stride=FRAME_OFFSET_STRIDE)
         self.planner.commit(self.publish)
-        self.offset.add_(FRAME_OFFSET_STRIDE)
         return self.tokens
 
     def capture(self, warmup: int = 2) -> None:
@@ -254,16 +276,21 @@ class TalkerDecodeStep:
     def replay(self) -> None:
         self.graph.replay()
 
-    def step(self, hidden: torch.Tensor) -> torch.Tensor:
-        """Host-facing step: ``hidden`` [batch, hidden] bf16 host tensor in,
-        sampled token ids (host int64 [batch]) out."""
+    def step(self, hidden: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Host-facing step: ``hidden`` [batch, hidden] bf16 host tensor in;
+        sampled token ids (host int64 [batch]) and terminal flags (host uint8
+        [batch], the device completion rule) out."""
 
         self._h_hidden.copy_(hidden)
         self.hidden_in.copy_(self._h_hidden, non_blocking=True)
         self.graph.replay()
         self._h_tokens.copy_(self.tokens, non_blocking=True)
+        self._h_terminal.copy_(self.control.terminal, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
-        return self._h_tokens
+        return self._h_tokens, self._h_terminal
+
+    def d2h_bytes(self) -> int:
+        return self.batch * (8 + 1)
 
     # ---------------------------------------------------------------- accounting
     def attention_bytes_per_layer(self) -> int:
@@ -343,20 +370,27 @@ class TalkerMixedStep:
         ends = torch.tensor(chunks).cumsum(0) - 1
         self._sample_rows = torch.cat([ends, self.t_pre + torch.arange(self.n_dec)]).to(dev)
         n = self.rows
-        self.temperature = torch.full((n,), 0.9, device=dev)
-        self.top_k = torch.full((n,), 50, dtype=torch.int32, device=dev)
-        self.top_p = torch.full((n,), 0.95, device=dev)
-        self.penalty = torch.full((n,), 1.05, device=dev)
-        self.seed = torch.arange(n, dtype=torch.long, device=dev)
-        self.offset = torch.zeros(n, dtype=torch.long, device=dev)
+        # request state on the device: row i serves request slot i
+        self.control = DeviceStepControl(slots=n, rows=n, device=dev, vocab=s.vocab, codec_vocab=s.codec_vocab,
+                                         eos_id=s.eos_id)
         self.seen = torch.zeros(n, s.vocab, dtype=torch.bool, device=dev)
         self.out_tokens = torch.zeros(n, dtype=torch.long, device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
         # parity hook: Exp(1) noise [rows, vocab] for the sampler's noise entry instead of the Philox draw
         self.sample_noise: torch.Tensor | None = None
 
+    temperature = property(lambda self: self.control.temperature)
+    top_k = property(lambda self: self.control.top_k)
+    top_p = property(lambda self: self.control.top_p)
+    penalty = property(lambda self: self.control.penalty)
+    seed = property(lambda self: self.control.seed)
+    offset = property(lambda self: self.control.offset)
+    terminal = property(lambda self: self.control.terminal)
+
     def admit(self, *, scatter_seed: int = 0) -> None:
-        """Prefill rows start empty; decode rows get their contexts on scattered pages."""
+        """Prefill rows start empty; decode rows get their contexts on scattered pages.  Every row samples
+        with T 0.9, top-k 50, top-p 0.95, penalty 1.05; prefill rows never terminate (their completion is
+        not a decode step, engine/pipeline.py:583-593), decode rows end on EOS."""
 
         P = self.page_size
         gen = torch.Generator().manual_seed(scatter_seed)
@@ -372,6 +406,11 @@ class TalkerMixedStep:
             dec_slots.append(slot)
         self.pre.set_rows(pre_slots, self.chunks)
         self.dec.set_rows(dec_slots, [1] * self.n_dec)
+        for i in range(self.rows):
+            prefill = i < self.n_pre
+            self.control.set_request(i, RequestSampling(0.9, 50, 0.95, 1.05, seed=i), max_tokens=EOS_NEVER,
+                                     eos_from_step=EOS_NEVER if prefill else eos_from(ignore_eos=False))
+        self.control.set_rows(list(range(self.rows)))
         ids = torch.randint(0, self.shape.vocab, (self.rows, 64), generator=gen)
         self.seen.zero_()
         self.seen.scatter_(1, ids.to(self.device), True)
@@ -383,6 +422,8 @@ class TalkerMixedStep:
         s, w = self.shape, self.weights
         hq, hkv, d = s.num_heads, s.num_kv_heads, s.head_dim
         tp, nd, T = self.t_pre, self.n_dec, self.tokens
+        ctl = self.control
+        ctl.stage()
         self.pre.plan(self.pre_b, prefill=True)
         self.dec.plan(self.dec_b, prefill=False)
         x, residual = self._x, self._residual
@@ -412,12 +453,13 @@ class TalkerMixedStep:
             x = _mlp_block(w, s, layer, o, residual, self._act)
             if trace is not None:
                 trace.append((x.clone(), residual.clone()))
-        logits = F.linear(x.index_select(0, self._sample_rows), w.w_head)
+        logits = ctl.mask_logits(F.linear(x.index_select(0, self._sample_rows), w.w_head))
         if trace is not None:
             trace.append(logits.clone())
-        sample_rows(logits, self.temperature, self.top_k, self.top_p, self.seed, self.offset,
-                    repetition_penalty=self.penalty, seen_token_mask=self.seen, update_seen=True,
+        sample_rows(logits, ctl.temperature, ctl.top_k, ctl.top_p, ctl.seed, ctl.offset,
+                    repetition_penalty=ctl.penalty, seen_token_mask=self.seen, update_seen=True,
                     round_scaled_to_input=False, noise=self.sample_noise, out=self.out_tokens)
+        ctl.finish(self.out_tokens, offset_stride=FRAME_OFFSET_STRIDE)
         self.pre.commit(False)
         self.dec.commit(False)
         # churn: churn_rows decode requests finish and new ones of the same lengths are admitted
@@ -430,7 +472,6 @@ class TalkerMixedStep:
                            prefill=True)
         self.adm.commit(True)
         self._churn_base.add_(self.churn_rows)
-        self.offset.add_(FRAME_OFFSET_STRIDE)
         return self.out_tokens
 
     def capture(self, warmup: int = 2) -> None:

@@ -14,6 +14,12 @@ and outputs as small torch files next to this script:
   planner.pt    PagedTalkerKV metadata (executor/talker_kv.py:403-533) and
                 allocator publications over a seeded script of add / prefill /
                 decode / publish / discard / remove operations.
+  binding.pt    what the reference's PagedTalkerKV hands a custom
+                binding_factory (executor/talker_kv.py:358-388) and every
+                metadata object it plans (prepare_prefill / prepare_decode /
+                prepare_capture, :485-533), recorded by a stand-in binding,
+                so the drop-in binding can be replayed against exactly
+                those calls without the reference installed.
   attention.pt  RMSNorm.forward + Qwen3TTSCodePredictor._apply_rope
                 (model/layers.py:103-115, model/components.py:214-233) on
                 bf16 heads, and _depth_attention (components.py:236-252) on
@@ -286,12 +292,66 @@ def make_attention(ref) -> dict:
     return out
 
 
+# ----------------------------------------------------------------------------- binding
+_META_FIELDS = ("qo_indptr", "paged_kv_indptr", "paged_kv_indices", "paged_kv_last_page_len", "position_ids",
+                "write_pages", "write_offsets", "padding_pages", "reuse_attention_plan")
+
+
+def make_binding(ref) -> dict:
+    """Drive the reference PagedTalkerKV through a prefill, three published
+    decode steps and a capture warm-up with a recording binding factory."""
+
+    import dataclasses
+
+    calls: list[dict] = []
+    factories: list[dict] = []
+
+    class Recorder:
+        def __init__(self, **kwargs) -> None:
+            self.index = len(factories)
+            factories.append({
+                "keys": sorted(kwargs),
+                "scalars": {k: v for k, v in kwargs.items() if isinstance(v, (int, float, bool)) or v is None},
+                "storage_shape": tuple(kwargs["storage"].shape),
+                "workspace_bytes": int(kwargs["workspace"].numel()),
+                "workspace_dtype": str(kwargs["workspace"].dtype),
+                "shared_plan_state": type(kwargs["shared_plan_state"]).__name__,
+                "dtype": str(kwargs["dtype"]),
+            })
+
+        def plan(self, metadata) -> None:
+            fields = [f.name for f in dataclasses.fields(metadata)]
+            entry = {"binding": self.index, "fields": fields}
+            for name in fields:
+                value = getattr(metadata, name)
+                entry[name] = value.clone() if isinstance(value, torch.Tensor) else value
+            calls.append(entry)
+
+    kv = ref["PagedTalkerKV"](num_layers=2, num_kv_heads=8, num_qo_heads=16, head_dim=128, total_pages=96,
+                              page_size=16, scratch_page_count=12, workspace_bytes=64 << 20,
+                              device=torch.device("cpu"), dtype=torch.bfloat16, binding_factory=Recorder)
+    for rid in ("a", "b", "c"):
+        kv.add_request(rid)
+    pkey = ref["TalkerPrefillCaptureKey"](4, 192, None)
+    pre = kv.create_prefill(pkey, slot=0)
+    for pub in kv.prepare_prefill(pre, pkey, ("a", "b", "c"), (40, 7, 100)):
+        pub.publish()
+    dkey = ref["TalkerDecodeCaptureKey"](4)
+    dec = kv.create_decode(dkey, slot=0)
+    for _ in range(3):
+        for pub in kv.prepare_decode(dec, dkey, ("a", "b", "c")):
+            pub.publish()
+    kv.abort(kv.prepare_capture(dec, dkey))
+    return {"factories": factories, "calls": calls, "metadata_fields": list(_META_FIELDS)}
+
+
 def main() -> None:
     ref = _import_reference()
     torch.save(make_sampler(ref), HERE / "sampler.pt")
     torch.save(make_planner(ref), HERE / "planner.pt")
     torch.save(make_attention(ref), HERE / "attention.pt")
-    for name in ("sampler.pt", "planner.pt", "attention.pt"):
+    torch.save(make_binding(ref), HERE / "binding.pt")
+    for name in ("sampler.pt", "planner.pt", "attention.pt", "binding.pt"):
         print(name, (HERE / name).stat().st_size, "bytes")
 
 

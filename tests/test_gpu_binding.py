@@ -198,3 +198,41 @@ def test_bindings_share_the_slot_workspace(nqt, cuda):
             pool.discard(r)
         storage_cpu.copy_(storage.cpu())
     assert nqt.kernels.read_status(cuda) == 0
+
+
+def test_binding_replays_the_reference_paged_talker_kv(nqt, cuda, golden):
+    """The calls the reference's own PagedTalkerKV makes on a custom binding
+    (factory kwargs, then plan() with its prefill / decode / capture metadata;
+    recorded by tests/golden/make_golden.py) replayed on B200TalkerBinding:
+    every plan is accepted and every attend matches the oracle."""
+
+    fx = golden("binding.pt")
+    shape = fx["factories"][0]["storage_shape"]
+    g = torch.Generator().manual_seed(8)
+    storage_cpu = torch.randn(*shape, generator=g).to(torch.bfloat16)
+    storage = storage_cpu.to(cuda)
+    workspace = torch.empty(fx["factories"][0]["workspace_bytes"], dtype=torch.uint8, device=cuda)
+    bindings = [nqt.binding_factory(storage=storage, workspace=workspace, shared_plan_state=object(), device=cuda,
+                                    dtype=torch.bfloat16, **f["scalars"]) for f in fx["factories"]]
+    attn = FakeAttention((1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).to(cuda),
+                         (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16).to(cuda))
+    for call in fx["calls"]:
+        binding = bindings[call["binding"]]
+        meta = nqt.TalkerAttentionMetadata(**{k: call[k] for k in call["fields"]})
+        binding.plan(meta)
+        prefill = meta.qo_indptr is not None
+        m = {k: (v.tolist() if isinstance(v, torch.Tensor) else v) for k, v in call.items()}
+        tokens = binding.token_capacity
+        valid = m["qo_indptr"][-1] if prefill else tokens
+        for layer in range(shape[0]):
+            binding.select_layer(layer)
+            qkv = torch.randn(tokens, 32 * 128, generator=g).to(torch.bfloat16)
+            q, k, v = (qkv[:, :2048].view(tokens, 16, 128), qkv[:, 2048:3072].view(tokens, 8, 128),
+                       qkv[:, 3072:].view(tokens, 8, 128))
+            want = _oracle_attend(storage_cpu[layer], m, q, k, v, attn, prefill)
+            qd = qkv.to(cuda)
+            got = binding.attend(attn, qd[:, :2048].view(tokens, 16, 128), qd[:, 2048:3072].view(tokens, 8, 128),
+                                 qd[:, 3072:].view(tokens, 8, 128))
+            torch.testing.assert_close(got[:valid].float().cpu(), want[:valid], atol=2e-2, rtol=0)
+        storage_cpu.copy_(storage.cpu())
+    assert nqt.kernels.read_status(cuda) == 0

@@ -170,7 +170,7 @@ def test_mixed_step_churn_keeps_the_pool_stationary(nqt, cuda):
     from importlib import import_module
 
     ts = import_module("nari-qwen3-tts_b200.talker_step")
-    shape = ts.TalkerShape(num_layers=2, hidden=256, ffn=512, vocab=512)
+    shape = ts.TalkerShape(num_layers=2, hidden=256, ffn=512, vocab=512, codec_vocab=384, eos_id=400)
     ctx = torch.randint(32, 400, (16,), generator=torch.Generator().manual_seed(4)).tolist()
     step = ts.TalkerMixedStep(shape=shape, chunks=[100, 37, 5], decode_contexts=ctx, churn_rows=4,
                               total_pages=2048, page_size=16, device=cuda, seed=0)

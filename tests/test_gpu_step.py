@@ -8,11 +8,14 @@ layer (the step's trace), so the check sees this layer's error only:
   * hidden state / residual after each layer: |err| <= 2e-2 + 2^-6 |want|
     and mean |err| <= 2e-3 (bf16 rounding at every module boundary plus the
     2e-2 attention tolerance);
-  * logits of the codec head: |err| <= 1e-2 + 2^-7 |want| (one bf16 rounding);
+  * logits of the codec head: |err| <= 1e-2 + 2^-7 |want| (one bf16 rounding), and the
+    suppress mask of forward_logits (columns past the code-predictor vocabulary
+    except EOS, and EOS on rows before step 2) exactly;
   * the K/V the step wrote: within 2^-7 relative + 1e-2;
   * sampled ids through the sampler's noise entry: bit-exact against the
     reference CPU sampler (oracle/sampler.py) on the step's logits, penalty
-    and seen mask; the seen mask and the RNG offsets after the step.
+    and seen mask; the seen mask, the terminal flags and the request slots'
+    step and RNG offset after the step.
 """
 
 from __future__ import annotations
@@ -23,6 +26,7 @@ import pytest
 import torch
 
 from oracle import sampler as osamp
+from oracle import step_control as octl
 from oracle import talker_step as ostep
 
 pytestmark = pytest.mark.gpu
@@ -64,6 +68,17 @@ def _meta(b, prefix=""):
     return out
 
 
+def _check_logits(step, got, hidden):
+    """Codec head + suppress mask of forward_logits against the oracle (first decode step: EOS suppressed)."""
+
+    s = step.shape
+    want = octl.mask_logits(ostep.head_logits(hidden, _cpu(step.weights.w_head)), s.codec_vocab, s.eos_id,
+                            [True] * got.shape[0])
+    finite = torch.isfinite(want)
+    assert torch.equal(torch.isfinite(got), finite) and bool((got[~finite] < 0).all())
+    _close(got[finite], want[finite], 1e-2, 2.0**-7, 1e-3, "codec head logits")
+
+
 def _check_layers(step, trace, storage0, meta, prefill_rows=0):
     shape, w = step.shape, step.weights
     x0, r0 = _cpu(trace[0][0]), _cpu(trace[0][1])
@@ -99,7 +114,8 @@ def test_talker_decode_step_matches_oracle(nqt, cuda):
     step.admit(contexts, scatter_seed=21)
     step.hidden_in.copy_(torch.randn(rows, shape.hidden, generator=g).to(torch.bfloat16).to(cuda))
     storage0 = step.storage.cpu()
-    seen0, off0 = step.seen.cpu(), step.offset.cpu()
+    ctl = step.control
+    seen0, off0, step0 = step.seen.cpu(), ctl.slot_offset.cpu(), ctl.slot_step.cpu()
     nqt.kernels.clear_status(cuda)
 
     trace: list = []
@@ -109,8 +125,8 @@ def test_talker_decode_step_matches_oracle(nqt, cuda):
     assert meta["pos"].tolist() == contexts  # one new token after each context
     _check_layers(step, trace, storage0, meta)
     logits = _cpu(trace[-1])
-    _close(logits, ostep.head_logits(_cpu(trace[-2][0]), _cpu(step.weights.w_head)), 1e-2, 2.0**-7, 1e-3,
-           "codec head logits")
+    _check_logits(step, logits, _cpu(trace[-2][0]))
+    assert torch.equal(step.offset.cpu(), off0)  # staged from the request slots
 
     # sampled ids through the noise entry: the oracle's Exp(1) noise, handed over by token id
     temp, top_k, top_p = step.temperature.cpu(), step.top_k.cpu(), step.top_p.cpu()
@@ -131,7 +147,8 @@ def test_talker_decode_step_matches_oracle(nqt, cuda):
                 noise[row, r] = d[3][i]
     # replay the same step (its reservation was discarded) with the noise entry
     step.seen.copy_(seen0.to(cuda))
-    step.offset.copy_(off0.to(cuda))
+    ctl.slot_offset.copy_(off0.to(cuda))
+    ctl.slot_step.copy_(step0.to(cuda))
     step.sample_noise = noise.to(cuda)
     trace2: list = []
     tokens = step.forward(trace2).cpu()
@@ -141,7 +158,9 @@ def test_talker_decode_step_matches_oracle(nqt, cuda):
     expect_seen = seen0.clone()
     expect_seen[torch.arange(rows), tokens] = True
     assert torch.equal(step.seen.cpu(), expect_seen)
-    assert torch.equal(step.offset.cpu(), off0 + ts.FRAME_OFFSET_STRIDE)
+    assert torch.equal(ctl.slot_offset.cpu(), off0 + ts.FRAME_OFFSET_STRIDE)
+    assert torch.equal(ctl.slot_step.cpu(), step0 + 1)
+    assert not bool(ctl.terminal.cpu().any())  # EOS is suppressed on the first steps, no limit
     assert nqt.kernels.read_status(cuda) == 0 and int(step.planner.status.item()) == 0
 
 
@@ -156,7 +175,7 @@ def test_talker_mixed_step_matches_oracle(nqt, cuda):
     step.admit(scatter_seed=31)
     step.hidden_in.copy_(torch.randn(step.tokens, shape.hidden, generator=g).to(torch.bfloat16).to(cuda))
     storage0 = step.storage.cpu()
-    seen0, off0 = step.seen.cpu(), step.offset.cpu()
+    seen0, off0 = step.seen.cpu(), step.control.slot_offset.cpu()
     nqt.kernels.clear_status(cuda)
 
     trace: list = []
@@ -168,7 +187,7 @@ def test_talker_mixed_step_matches_oracle(nqt, cuda):
     final = _cpu(trace[-2][0])
     sampled = final.index_select(0, step._sample_rows.cpu())
     logits = _cpu(trace[-1])
-    _close(logits, ostep.head_logits(sampled, _cpu(step.weights.w_head)), 1e-2, 2.0**-7, 1e-3, "codec head logits")
+    _check_logits(step, logits, sampled)
     # the production draw: every sampled id lies in the reference sampler's filtered support
     details = osamp.row_details(logits, step.temperature.cpu(), step.top_k.cpu(), step.top_p.cpu(), step.seed.cpu(),
                                 off0, repetition_penalty=step.penalty.cpu(), seen_token_mask=seen0)
@@ -178,5 +197,6 @@ def test_talker_mixed_step_matches_oracle(nqt, cuda):
     expect_seen = seen0.clone()
     expect_seen[torch.arange(step.rows), tokens] = True
     assert torch.equal(step.seen.cpu(), expect_seen)
-    assert torch.equal(step.offset.cpu(), off0 + ts.FRAME_OFFSET_STRIDE)
+    assert torch.equal(step.control.slot_offset.cpu(), off0 + ts.FRAME_OFFSET_STRIDE)
+    assert not bool(step.control.terminal.cpu().any())
     assert nqt.kernels.read_status(cuda) == 0
