@@ -21,7 +21,11 @@ Reported on the JSON line besides the throughput:
                seen-mask bytes / duration vs the measured HBM copy peak;
   cpu_baseline whole steps of the CPU port (oracle/talker_step.py: every
                layer, every row) for about --cpu-seconds (rank 0, N = 1);
-  clocks       nvidia-smi samples taken during the timed region.
+  clocks       nvidia-smi samples taken during the timed region;
+  config4_mixed, config3_code_predictor
+               at N = 1, the mixed continuous batch and
+               the code-predictor frame (config 3) measured in the same run
+               (the --workload mixed / cp lines, summarised).
 ``--impl reference`` times whole steps of the CPU port alone (the reference
 arm), on rank 0 only at every N.
 """
@@ -62,6 +66,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--pool-tokens", type=int, default=POOL_TOKENS)
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-other-configs", action="store_true",
+                   help="headline run only: skip the config-3 / config-4 measurements carried on its line")
     p.add_argument("--grow", action="store_true",
                    help="publish each step (contexts grow by one token per step) instead of holding them fixed")
     return p.parse_args()
@@ -266,7 +272,7 @@ def time_graph(fn, reps: int, stream) -> float:
     return a0.elapsed_time(a1) / reps
 
 
-def run_mixed(args, world, rank, local) -> None:
+def run_mixed(args, world, rank, local, emit: bool = True) -> dict:
     """8 chunked prefills U[128, 1024] + 240 decode rows ctx U[32, 4096], GPU planner each
     step, 10 % of the sequences finish and are replaced each step (on the device)."""
 
@@ -358,15 +364,16 @@ def run_mixed(args, world, rank, local) -> None:
         "clocks": clocks.summary(),
         "device_status": status,
     }
-    if rank == 0:
+    if emit and rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
+    if emit and world > 1:
         import torch.distributed as dist
 
         dist.destroy_process_group()
+    return line
 
 
-def run_cp(args, world, rank, local) -> None:
+def run_cp(args, world, rank, local, emit: bool = True) -> dict:
     """one code-predictor frame (15 residual codebooks, each with its own 2048-way head and
     sampler call) for B=256 rows, 5-layer decoder, hidden 1024, 16/8 heads, D 64, FFN 3072, top-k 50, T 0.9."""
 
@@ -483,7 +490,7 @@ def run_cp(args, world, rank, local) -> None:
         "clocks": clocks.summary(),
         "device_status": status,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if emit and rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle.code_predictor import CpuCodePredictorFrame
 
         threads = os.cpu_count() or 1
@@ -501,12 +508,13 @@ def run_cp(args, world, rank, local) -> None:
             "sample": f"{len(times)} whole frames of {sample_rows_cpu} rows through the CPU port "
                       "(oracle/code_predictor.py: bf16-rounded activations, fp32 math, reference CPU sampler)",
         }
-    if rank == 0:
+    if emit and rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
+    if emit and world > 1:
         import torch.distributed as dist
 
         dist.destroy_process_group()
+    return line
 
 
 class SamplerWorkload:
@@ -636,6 +644,16 @@ def run_sampler(args, world, rank, local) -> None:
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+def _summary(line: dict) -> dict:
+    """The parts of another workload's bench line carried on the headline line."""
+
+    keys = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "e2e", "roofline", "decode_roofline",
+            "decode_seq_steps_per_s", "sampler_us_per_launch", "gpu_launches", "clocks", "device_status")
+    out = {k: line[k] for k in keys if k in line}
+    out["workload"] = line["config"]["workload"]
+    return out
 
 
 def main() -> None:
@@ -790,11 +808,19 @@ def main() -> None:
         "clocks": clocks.summary(),
         "device_status": status,
     }
+    del ag, attention_pass, b, step, q, outs
+    if world == 1 and args.layers == 28 and not args.no_other_configs:
+        # BASELINE configs 3 and 4 on the same GPU, after the config-2 step's memory is released
+        torch.cuda.empty_cache()
+        sub = argparse.Namespace(**{**vars(args), "steps": min(args.steps, 20), "warmup": min(args.warmup, 3)})
+        line["config4_mixed"] = _summary(run_mixed(sub, world, rank, local, emit=False))
+        torch.cuda.empty_cache()
+        line["config3_code_predictor"] = _summary(run_cp(sub, world, rank, local, emit=False))
+        torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds, shape.num_layers)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del ag, step
     if world > 1:
         import torch.distributed as dist
 
