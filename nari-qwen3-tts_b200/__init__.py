@@ -7,7 +7,7 @@ name is not a Python identifier).  Kernels live in ``libnqt.so`` (C ABI in
 include/nqt.h); build it with ``build.build()``.
 """
 
-from . import kernels, planner, sampling, talker_kv
+from . import kernels, planner, sampling, step_control, talker_kv
 from ._lib import NqtError, lib
 from .kernels import (
     cp_decode_attention_,
@@ -24,6 +24,7 @@ from .sampling import (
     sample_rows,
     sample_talker_cuda_graph,
 )
+from .step_control import DeviceStepControl, RequestSampling
 from .talker_kv import (
     B200TalkerBinding,
     TalkerAttentionMetadata,
@@ -35,8 +36,10 @@ from .talker_kv import (
 __all__ = [
     "B200TalkerBinding",
     "DevicePagePlanner",
+    "DeviceStepControl",
     "KVAllocationError",
     "NqtError",
+    "RequestSampling",
     "TalkerAttentionMetadata",
     "batch_decode_paged",
     "batch_prefill_paged",
@@ -55,5 +58,6 @@ __all__ = [
     "sample_rows",
     "sample_talker_cuda_graph",
     "sampling",
+    "step_control",
     "talker_kv",
 ]
