@@ -110,8 +110,10 @@ class CodePredictorFrame:
         groups = torch.arange(1, self.shape.groups, device=self.device)
         self.offsets.copy_((frame_index * FRAME_STRIDE + groups * CODEBOOK_STRIDE).unsqueeze(0).expand(self.rows, -1))
 
-    def _depth_step(self, x: torch.Tensor, cache_pos: int, final_norm: bool) -> torch.Tensor:
-        """Five layers on one token per row at `cache_pos` (model/components.py:254-356)."""
+    def _depth_step(self, x: torch.Tensor, cache_pos: int, final_norm: bool,
+                    residuals: list | None = None) -> torch.Tensor:
+        """Five layers on one token per row at `cache_pos` (model/components.py:254-356).
+        ``residuals`` (parity tests) receives the residual stream before each layer and after the last."""
 
         s = self.shape
         hq, hkv, d = s.num_heads, s.num_kv_heads, s.head_dim
@@ -120,6 +122,8 @@ class CodePredictorFrame:
         residual.copy_(x)
         h = kernels.rmsnorm(x, self.ln_in[0], s.eps)
         for layer in range(s.num_layers):
+            if residuals is not None:
+                residuals.append(residual.clone())
             qkv = F.linear(h, self.w_qkv[layer])
             q = qkv[:, : hq * d].view(rows, hq, d)
             k = qkv[:, hq * d: (hq + hkv) * d].view(rows, hkv, d)
@@ -135,20 +139,37 @@ class CodePredictorFrame:
             last = layer + 1 == s.num_layers
             if last and not final_norm:
                 residual.add_(m)
+                if residuals is not None:
+                    residuals.append(residual.clone())
                 return residual
             kernels.fused_add_rmsnorm_(m, residual, self.ln_final if last else self.ln_in[layer + 1], s.eps)
             h = m
+        if residuals is not None:
+            residuals.append(residual.clone())
         return h
 
-    def forward(self) -> torch.Tensor:
+    def forward(self, trace: list | None = None) -> torch.Tensor:
+        """The frame body (what capture() records).  ``trace``, for parity tests
+        of an eager frame: receives per depth step (the residual stream before
+        each layer and after the last, a copy of the frame cache before the
+        step, the output hidden state or None for position 0)."""
+
         s = self.shape
         hidden0 = F.linear(self.past_hidden, self.w_in, self.b_in)
-        self._depth_step(hidden0, 0, final_norm=False)
+        residuals = [] if trace is not None else None
+        cache_before = self.kv_cache.clone() if trace is not None else None
+        self._depth_step(hidden0, 0, final_norm=False, residuals=residuals)
+        if trace is not None:
+            trace.append((residuals, cache_before, None))
         self.frames[:, 0].copy_(self.layer0_token)
         self.codec_sum.copy_(F.embedding(self.layer0_token, self.layer0_embedding))
         x = F.embedding(self.layer0_token, self.projected_layer0)
         for group in range(1, s.groups):
-            hidden = self._depth_step(x, group, final_norm=True)
+            cache_before = self.kv_cache.clone() if trace is not None else None
+            residuals = [] if trace is not None else None
+            hidden = self._depth_step(x, group, final_norm=True, residuals=residuals)
+            if trace is not None:
+                trace.append((residuals, cache_before, hidden.clone()))
             logits = torch.matmul(hidden, self.lm_head[group - 1].t(), out=self.logits[group - 1])
             sample_rows(logits, self.temperature, self.top_k, self.top_p, self.seed, self.offsets[:, group - 1],
                         round_scaled_to_input=False, out=self._token)

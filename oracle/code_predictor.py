@@ -75,27 +75,35 @@ class CpuCodePredictorFrame:
         return cls(weights, heads=heads, kv_heads=kv_heads, head_dim=head_dim, groups=groups)
 
     def _depth_step(self, x: torch.Tensor, cache: list, cache_pos: int, final_norm: bool) -> torch.Tensor:
+        for layer in range(self.layers):
+            x = self.depth_layer(x, layer, cache, cache_pos)
+        return _rms(x, self.w["ln_final"], self.eps) if final_norm else x
+
+    def depth_layer(self, x: torch.Tensor, layer: int, cache: list, cache_pos: int) -> torch.Tensor:
+        """One decoder layer of a depth step on the residual stream x (model/components.py:300-350):
+        RMSNorm, QKV, QK norm + RoPE + dense cache write, short-cache attention, O, residual add (rounded),
+        RMSNorm, gate/up, SiLU * up, down, residual add.  Writes cache[layer] at cache_pos."""
+
         w = self.w
         rows = x.shape[0]
         hq, hkv, d = self.heads, self.kv_heads, self.head_dim
         positions = torch.full((rows,), cache_pos, dtype=torch.long)
-        for layer in range(self.layers):
-            h = _rms(x, w["ln_in"][layer], self.eps)
-            qkv = _bf(h @ w["w_qkv"][layer].T)
-            q = qkv[:, : hq * d].reshape(rows, hq, d).to(BF16)
-            k = qkv[:, hq * d: (hq + hkv) * d].reshape(rows, hkv, d).to(BF16)
-            v = qkv[:, (hq + hkv) * d:].reshape(rows, hkv, d).to(BF16)
-            kc, vc = cache[layer]
-            oatt.qk_norm_rope_dense_(q, k, v, w["q_norm"][layer].to(BF16), w["k_norm"][layer].to(BF16), positions,
-                                     self.eps, self.theta, kc, vc, cache_pos, round_to_input=False)
-            attn = _bf(oatt.short_cache_attention(q, kc, vc, cache_pos + 1))
-            x = _bf(x + _bf(attn.reshape(rows, hq * d) @ w["w_o"][layer].T))
-            h = _rms(x, w["ln_post"][layer], self.eps)
-            gu = _bf(h @ w["w_gate_up"][layer].T)
-            ffn = gu.shape[1] // 2
-            act = _bf(F.silu(gu[:, :ffn]) * gu[:, ffn:])
-            x = _bf(x + _bf(act @ w["w_down"][layer].T))
-        return _rms(x, w["ln_final"], self.eps) if final_norm else x
+        h = _rms(x, w["ln_in"][layer], self.eps)
+        qkv = _bf(h @ w["w_qkv"][layer].T)
+        q = qkv[:, : hq * d].reshape(rows, hq, d).to(BF16)
+        k = qkv[:, hq * d: (hq + hkv) * d].reshape(rows, hkv, d).to(BF16)
+        v = qkv[:, (hq + hkv) * d:].reshape(rows, hkv, d).to(BF16)
+        kc, vc = cache[layer]
+        oatt.qk_norm_rope_dense_(q, k, v, w["q_norm"][layer].to(BF16), w["k_norm"][layer].to(BF16), positions,
+                                 self.eps, self.theta, kc, vc, cache_pos, round_to_input=False)
+        attn = _bf(oatt.short_cache_attention(q, kc, vc, cache_pos + 1))
+        x = _bf(x + _bf(attn.reshape(rows, hq * d) @ w["w_o"][layer].T))
+        h = _rms(x, w["ln_post"][layer], self.eps)
+        gu = _bf(h @ w["w_gate_up"][layer].T)
+        ffn = gu.shape[1] // 2
+        act = _bf(F.silu(gu[:, :ffn]) * gu[:, ffn:])
+        x = _bf(x + _bf(act @ w["w_down"][layer].T))
+        return x
 
     def frame(self, past_hidden, layer0_token, *, temperature, top_k, top_p, seed, offsets, forced_tokens=None):
         """Returns (frames [rows, groups], logits [groups-1, rows, vocab] fp32, codec_sum fp32)."""
