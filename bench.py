@@ -60,8 +60,11 @@ def parse() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=300)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("decode", "mixed", "cp", "sampler"), default="decode",
-                   help="decode = BASELINE config 2 (the headline); mixed = config 4 (prefill chunks + decode rows)")
+    p.add_argument("--workload", choices=("decode", "mixed", "cp", "sampler", "serve"), default="decode",
+                   help="decode = BASELINE config 2 (the headline); mixed = config 4 (prefill chunks + decode rows); "
+                        "cp = config 3; serve = config 5 (box serving simulation); sampler = the sampler roofline")
+    p.add_argument("--serve-seconds", type=float, default=10.0, help="config 5: arrival window per GPU (s)")
+    p.add_argument("--serve-rps", type=float, default=20.0, help="config 5: Poisson arrival rate per GPU")
     p.add_argument("--layers", type=int, default=28, help="decoder layers (28 = BASELINE config 2)")
     p.add_argument("--pool-tokens", type=int, default=POOL_TOKENS)
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
@@ -656,6 +659,87 @@ def _summary(line: dict) -> dict:
     return out
 
 
+def run_serve(args, world, rank, local) -> None:
+    """box-level request-sharded serving simulation.  Poisson arrivals (args.serve_rps per
+    GPU, seeded) are routed round-robin to the ranks; each rank is one ServingWorker (64 request slots, its own
+    page pool, GPU planner, device request table, talker decode step and code-predictor frame, all captured);
+    text 20-200 tokens of prefill, 2-20 s of audio at 12 frames/s.  Reported: frames/s per box (sum over
+    ranks / the slowest rank's wall time) and time-to-first-frame percentiles over every request."""
+
+    from importlib import import_module
+
+    serving = import_module("nari-qwen3-tts_b200.serving")
+    talker_step = import_module("nari-qwen3-tts_b200.talker_step")
+    nqt = import_module("nari-qwen3-tts_b200")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    shape = talker_step.TalkerShape(num_layers=args.layers)
+    worker = serving.ServingWorker(shape=shape, slots=BATCH, pool_tokens=128 * 1024, device=dev, seed=rank)
+    worker.capture()
+    requests = serving.poisson_requests(rate=args.serve_rps, horizon=args.serve_seconds, seed=5000, rank=rank,
+                                        world=world)
+    torch.cuda.synchronize()
+    barrier(world)
+    with ClockSampler(dev) as clocks:
+        rep = worker.run(requests, horizon=args.serve_seconds)
+    barrier(world)
+    elapsed = max_over_ranks(rep.elapsed, world)
+    local_stats = torch.tensor([rep.frames, rep.steps, rep.finished, rep.admitted, len(requests)], dtype=torch.float64)
+    ttff = torch.tensor(rep.ttff, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(local_stats)
+        sizes = [torch.zeros(1, dtype=torch.long) for _ in range(world)]
+        dist.all_gather(sizes, torch.tensor([ttff.numel()]))
+        width = int(max(x.item() for x in sizes))
+        padded = torch.full((width,), float("nan"), dtype=torch.float64)
+        padded[: ttff.numel()] = ttff
+        gathered = [torch.empty(width, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(gathered, padded)
+        ttff = torch.cat(gathered)
+        ttff = ttff[~torch.isnan(ttff)]
+    frames, steps, finished, admitted, offered = (float(x) for x in local_stats)
+    q = (lambda p: float(torch.quantile(ttff, p)) * 1e3) if ttff.numel() else (lambda p: None)
+    status = nqt.kernels.read_status(dev) | int(worker.step.planner.status.item())
+    line = {
+        "metric": "box serving frames/s (talker + code predictor, Poisson arrivals per GPU)",
+        "value": frames / elapsed,
+        "unit": "frames/s",
+        "n_gpus": world,
+        "steps": int(rep.steps),
+        "warmup": 1,
+        "ms_per_step": rep.elapsed / max(rep.steps, 1) * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init bf16 weights; seeded Poisson arrivals, text and audio lengths)",
+        "config": {
+            "workload": f"BASELINE config 5: {args.serve_rps:g} RPS per GPU for {args.serve_seconds:g} s, text 20-200 "
+                        f"tokens, audio 2-20 s at 12 frames/s; per GPU 64 request slots, {shape.num_layers}-layer talker "
+                        "+ 5-layer code predictor, one page pool, GPU planner and device request table",
+            "global_batch": world * BATCH,
+            "seq_len": 256 + 240,
+            "parallelism": f"dp{world} (request-sharded: round-robin router, no collective)",
+            "timing": "host wall clock over the arrival window plus the drain, each step synchronised",
+        },
+        "p50_ttff_ms": q(0.5),
+        "p95_ttff_ms": q(0.95),
+        "requests": {"offered": int(offered), "admitted": int(admitted), "finished": int(finished)},
+        "frames": int(frames),
+        "mean_busy_rows_rank0": sum(rep.busy_rows) / max(len(rep.busy_rows), 1),
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main() -> None:
     args = parse()
     world, rank, local = dist_setup(args)
@@ -670,6 +754,9 @@ def main() -> None:
         return
     if args.workload == "sampler":
         run_sampler(args, world, rank, local)
+        return
+    if args.workload == "serve":
+        run_serve(args, world, rank, local)
         return
     nqt = importlib.import_module("nari-qwen3-tts_b200")
     from importlib import import_module

@@ -248,6 +248,7 @@ class TalkerDecodeStep:
             x = _mlp_block(w, s, layer, o, residual, self._act)
             if trace is not None:
                 trace.append((x.clone(), residual.clone()))
+        self.last_hidden = x  # the final normed hidden state (the code predictor's input)
         logits = ctl.mask_logits(F.linear(x, w.w_head))
         if trace is not None:
             trace.append(logits.clone())
