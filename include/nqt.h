@@ -436,6 +436,63 @@ int nqt_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, void* y, int
                   int m, int n, int k, int epilogue, int split, int32_t* status, void* stream);
 
 /*
+ * FP8 (e4m3) block-scaled gate/up projection.  The reference's production
+ * executor requires it for every talker layer (executor/build.py:73,
+ * executor/optimizations.py:22-47), on a path that only starts on sm90.
+ *
+ * nqt_fp8_quantize_weight_blocks replaces quantize_fp8_weight_blocks
+ * (model/layers.py:11-25): per 128 x 128 block of the bf16 weight [n, k],
+ * s = 2^ceil(log2(max(amax, 1e-4) / 448)) and q = e4m3(w / s).  Outputs in
+ * the reference's layout: q [n, k] row-major (ldq bytes), scale f32
+ * [n / 128, k / 128].  n, k multiples of 128.
+ *
+ * nqt_fp8_quantize_rows is the activation rule of the reference's GEMM on a
+ * bf16 input (model/layers.py:242-256, flashinfer fp8_blockscale_gemm_sm90:
+ * per token per 128-element block, f = 448 / amax or 1 when amax = 0,
+ * q = e4m3(x * f), scale = 1 / f).  q [m, k] (ldq bytes); scale f32
+ * K-block-major: scale[b * ld_scale + row], ld_scale >= m.
+ *
+ * nqt_fused_add_rmsnorm_fp8 is nqt_fused_add_rmsnorm (bf16) whose output row
+ * is quantised by that rule into q / scale (same layouts); the bf16 normed
+ * row is also written to x when write_x != 0.  hidden % 128 == 0.
+ *
+ * nqt_gemm_fp8_pack_weight lays q out once as 16 KB units [n / 128][k / 128]
+ * [128 rows x 128 B] in the MMA's swizzled order (interleave_gate_up: unit
+ * rows in 32-row groups [gate 16 | up 16], so unit t holds gate and up rows
+ * 64 t .. 64 t + 63 of a weight [gate (n/2 rows) | up (n/2 rows)]).
+ *
+ * nqt_gemm_fp8: Y = sum over K blocks b of (Xq_b . Wq_b^T) * xscale[b, row] *
+ * wscale[weight row / 128, b] (fp32), epilogue 0 (Y = bf16) or 2 (packed with
+ * interleave_gate_up: Y[m, f] = silu(bf16 g) * bf16 up, Y is [m, n / 2]).
+ * wscale is the quantiser's [n / 128, k / 128] table in the unpacked row
+ * order.  m >= 1 (chunks of up to 128 tokens), n % 128 == 0 (n % 256 with
+ * interleave_gate_up), k % 128 == 0; xq and the packed weight 16-byte
+ * aligned, ldxq a multiple of 16.  split bits 0-7: CTAs that share each
+ * tile's K, 1..8, 0 = automatic (every SM streams about the same number of
+ * K blocks); bits 8-11: K blocks per copy stage, 0 = automatic.  A split
+ * sums its fp32 partials through `workspace` (256-byte aligned, at least
+ * nqt_gemm_fp8_workspace_bytes for the same m, n, k and split; none is needed
+ * when that is 0): zero it once before the first call; every launch returns
+ * its tickets to zero.  A workspace's tickets are laid out for one (m, n, k,
+ * split): give each shape its own workspace (or zero it before another
+ * shape uses it), and run one launch at a time per workspace.  Launched with
+ * programmatic stream serialization.
+ */
+int nqt_fp8_quantize_weight_blocks(const void* w, int64_t ldw, int n, int k, void* q, int64_t ldq, float* scale,
+                                   void* stream);
+int nqt_fp8_quantize_rows(const void* x, int64_t ldx, int m, int k, void* q, int64_t ldq, float* scale,
+                          int64_t ld_scale, void* stream);
+int nqt_fused_add_rmsnorm_fp8(void* x, void* residual, const void* weight, int rows, int hidden, float eps, void* q,
+                              int64_t ldq, float* scale, int64_t ld_scale, int write_x, int dtype, void* stream);
+int nqt_gemm_fp8_pack_weight(const void* q, int64_t ldq, int n, int k, int interleave_gate_up, void* packed,
+                             void* stream);
+int nqt_gemm_fp8_workspace_bytes(int m, int n, int k, int split, int64_t* bytes);
+int nqt_gemm_fp8(const void* xq, int64_t ldxq, const float* xscale, int64_t ld_xscale, const void* w_packed,
+                 const float* wscale, void* y, int64_t ldy, int m, int n, int k, int epilogue,
+                 int interleave_gate_up, int split, void* workspace, int64_t workspace_bytes, int32_t* status,
+                 void* stream);
+
+/*
  * Device-side request control of a talker step (no host staging before a captured step, no per-row
  * host read after it).  Per-request state lives in a slot table on the device; rows name their slot
  * (row_slot[r] < 0 marks a padding row).  Distinct rows must name distinct slots.

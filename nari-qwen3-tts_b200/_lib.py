@@ -96,6 +96,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqt_silu_and_mul": (I, [P, L, P, L, I, I, I, P]),
     "nqt_gemm_pack_weight": (I, [P, L, I, I, I, P, P]),
     "nqt_gemm_bf16": (I, [P, L, P, P, L, P, I, I, I, I, I, P, P]),
+    "nqt_fp8_quantize_weight_blocks": (I, [P, L, I, I, P, L, P, P]),
+    "nqt_fp8_quantize_rows": (I, [P, L, I, I, P, L, P, L, P]),
+    "nqt_fused_add_rmsnorm_fp8": (I, [P, P, P, I, I, F, P, L, P, L, I, I, P]),
+    "nqt_gemm_fp8_pack_weight": (I, [P, L, I, I, I, P, P]),
+    "nqt_gemm_fp8_workspace_bytes": (I, [I, I, I, I, P]),
+    "nqt_gemm_fp8": (I, [P, L, P, L, P, P, P, L, I, I, I, I, I, I, P, L, P, P]),
     "nqt_step_stage": (I, [P, I, I, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
     "nqt_talker_logits_mask": (I, [P, I, L, I, I, I, I, P, P]),
     "nqt_step_finish": (I, [P, I, I, P, I, P, P, P, P, L, P, P, P, P]),

@@ -42,15 +42,16 @@
 // Replaces the torch/cuBLAS projections of the decoder layers
 // (model/layers.py:195-270, model/components.py:300-356) and the sm90-only
 // fused gate/up path (executor/optimizations.py:22-47).
-#include <cudaTypedefs.h>
-
 #include <mutex>
 
 #include "common.cuh"
+#include "gemm_common.cuh"
 #include "tcgen05.cuh"
 
 namespace nqt {
 namespace {
+
+using namespace gemm_detail;
 
 constexpr int kTileN = 128;                    // W rows per tile (MMA M)
 constexpr int kBlockK = 64;                    // K per unit (one 128-byte swizzle row)
@@ -93,73 +94,6 @@ __host__ __device__ constexpr int ring_bytes(int mpad, int group, int m, int S, 
   return stages * stage_bytes(mpad, group) > park_bytes(m, S) ? stages * stage_bytes(mpad, group)
                                                                : park_bytes(m, S);
 }
-
-// Contiguous global -> shared copy completing on an mbarrier (16-byte aligned, size % 16 == 0).
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_addr(dst)),
-               "l"(src), "r"(bytes), "r"(smem_addr(bar))
-               : "memory");
-}
-
-// X slabs [c2, c2 + group) of the 3-D view {64 k, m rows, k / 64 slabs} (one copy per stage)
-__device__ __forceinline__ void tma_load_x(void* dst, const CUtensorMap* map, uint64_t* bar, int slab) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(0), "r"(0), "r"(slab)
-      : "memory");
-}
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Cluster barrier, split: every thread of every CTA arrives once, then waits once (release / acquire at
-// cluster scope), alternating.  Whole converged warps only (.aligned): call sites reconverge first.
-__device__ __forceinline__ void cluster_arrive() {
-  __syncwarp();
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-  __syncwarp();
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-  __syncwarp();
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Contiguous copy from this CTA's shared memory into a peer's, completing `bar_cluster_addr`'s
-// transaction count there (16-byte aligned, size % 16 == 0).
-__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster_addr, const void* src, uint32_t bytes,
-                                                  uint32_t bar_cluster_addr) {
-  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   dst_cluster_addr),
-               "r"(smem_addr(src)), "r"(bytes), "r"(bar_cluster_addr)
-               : "memory");
-}
-
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// Address of the same shared-memory offset in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
-  return v;
-}
-
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + __expf(-g)) * u; }
-
-__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap xmap, GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -211,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
     prefetch_tensormap(&xmap);
     grid_dependency_wait();
-    for (int i = 0; i < pro; ++i) tma_load_x(smem + i * sb + xoff, &xmap, &full[i], kb0 + i * G);
+    for (int i = 0; i < pro; ++i) tma_load_x(smem + i * sb + xoff, &xmap, &full[i], 0, kb0 + i * G);
   }
   // the next kernel may be scheduled now and stream its own weights while this one finishes
   grid_dependents_launch();
@@ -239,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         const int g = nu - i * G < G ? nu - i * G : G;
         mbar_arrive_expect_tx(&full[s], g * kWBytes + G * x_bytes(a.mpad));
         bulk_load(smem + s * sb, wsrc + static_cast<int64_t>(i) * G * kWBytes, g * kWBytes, &full[s]);
-        tma_load_x(smem + s * sb + xoff, &xmap, &full[s], kb0 + i * G);
+        tma_load_x(smem + s * sb + xoff, &xmap, &full[s], 0, kb0 + i * G);
       }
     }
     cluster_wait();
@@ -409,37 +343,6 @@ __global__ void pack_kernel(const __nv_bfloat16* w, int64_t ldw, int n, int k, i
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
-// 2-D K-major map of a row-major bf16 matrix [rows, cols] with leading dimension ld, box {64, box_rows}.
-// X [rows, cols] (row pitch ld) viewed as {64 k, rows, cols / 64 slabs} with box {64, box_rows, group}: one
-// copy brings `group` K slabs, each [box_rows x 128 B] with the 128-byte swizzle, one after another.
-int encode_x(CUtensorMap* map, const void* base, int rows, int cols, int64_t ld, int box_rows, int group) {
-  auto encode = get_encode();
-  if (encode == nullptr) return NQT_ERR_CUDA;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kBlockK), static_cast<cuuint64_t>(rows),
-                        static_cast<cuuint64_t>(cols / kBlockK)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(kBlockK) * 2};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(box_rows),
-                       static_cast<cuuint32_t>(group)};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? NQT_OK : NQT_ERR_CUDA;
-}
-
 int smem_bytes(int mpad, int group, int m, int S, int stages) {
   return 1024 + ring_bytes(mpad, group, m, S, stages) + recv_bytes(m, S) + (2 * stages + 2) * 8 + 16;
 }
@@ -564,7 +467,8 @@ extern "C" int nqt_gemm_bf16(const void* x, int64_t ldx, const void* wpacked, vo
   }
 
   CUtensorMap xmap;
-  if (encode_x(&xmap, x, m, k, ldx, mpad, pl.group) != NQT_OK) {
+  if (encode_x_slabs(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, m, k / kBlockK, ldx * 2, mpad, pl.group) !=
+      NQT_OK) {
     set_last_message("gemm: cuTensorMapEncodeTiled failed");
     return NQT_ERR_CUDA;
   }

@@ -6,7 +6,12 @@
 //   fused_add_rmsnorm:  r = x + residual (fp32); residual <- r;
 //                       x <- r * rsqrt(mean(r^2) + eps) * w             (flashinfer.norm.fused_add_rmsnorm)
 //   silu_and_mul:       out = silu(g) * u for gate_up = [g | u]          (flashinfer.activation.silu_and_mul)
+//   fused_add_rmsnorm_fp8: fused_add_rmsnorm whose bf16 output is quantised to e4m3 per 128-element block
+//                       (the activation rule of the reference's FP8 gate/up GEMM, fp8.cuh) for the FP8
+//                       gate/up GEMM that follows; it lets that GEMM be scheduled at once (PDL) so the
+//                       weight stream starts while the norm runs.
 #include "common.cuh"
+#include "fp8.cuh"
 
 namespace nqt {
 namespace {
@@ -109,6 +114,66 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(T* x, T* resi
   }
 }
 
+// add_rmsnorm for bf16 rows with hidden % 128 == 0; the normed row is rounded to bf16, then each
+// 128-element block (16 vectors = 16 consecutive lanes) is quantised to e4m3 with its own scale.
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_fp8_kernel(__nv_bfloat16* x, __nv_bfloat16* residual,
+                                                                       const __nv_bfloat16* w, int hidden, float eps,
+                                                                       uint8_t* q, int64_t ldq, float* scale,
+                                                                       int64_t ld_scale, int write_x) {
+  grid_dependents_launch();  // the FP8 GEMM after this kernel may start streaming its weights
+  const int row = blockIdx.x;
+  const int nvec = hidden / 8;
+  float r[kMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    const int i = threadIdx.x + j * kNormThreads;
+    if (i < nvec) {
+      Vec8<__nv_bfloat16> a, b, o;
+      a.raw = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(row) * hidden)[i];
+      b.raw = reinterpret_cast<const uint4*>(residual + static_cast<int64_t>(row) * hidden)[i];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        r[j][e] = a.get(e) + b.get(e);
+        ss += r[j][e] * r[j][e];
+        o.set(e, r[j][e]);
+      }
+      reinterpret_cast<uint4*>(residual + static_cast<int64_t>(row) * hidden)[i] = o.raw;
+    }
+  }
+  const float inv = rsqrtf(block_sum(ss) / hidden + eps);
+#pragma unroll
+  for (int j = 0; j < kMaxVec; ++j) {
+    if (j * kNormThreads >= nvec) break;  // uniform over the CTA
+    const int i = threadIdx.x + j * kNormThreads;
+    Vec8<__nv_bfloat16> o;
+    float v[8];
+    float amax = 0.f;
+    if (i < nvec) {
+      Vec8<__nv_bfloat16> wv;
+      wv.raw = reinterpret_cast<const uint4*>(w)[i];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        o.set(e, r[j][e] * inv * wv.get(e));
+        v[e] = o.get(e);
+        amax = fmaxf(amax, fabsf(v[e]));
+      }
+    }
+    // whole 16-lane groups are valid or not (nvec % 16 == 0)
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, off));
+    if (i < nvec) {
+      const float f = fp8::act_block_factor(amax);
+      uint2 pk;
+      pk.x = fp8::e4m3x4(v[0] * f, v[1] * f, v[2] * f, v[3] * f);
+      pk.y = fp8::e4m3x4(v[4] * f, v[5] * f, v[6] * f, v[7] * f);
+      *reinterpret_cast<uint2*>(q + static_cast<int64_t>(row) * ldq + i * 8) = pk;
+      if ((i & 15) == 0) scale[static_cast<int64_t>(i >> 4) * ld_scale + row] = __fdiv_rn(1.f, f);
+      if (write_x) reinterpret_cast<uint4*>(x + static_cast<int64_t>(row) * hidden)[i] = o.raw;
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads) silu_mul_kernel(const T* gu, int64_t gs, T* out, int64_t os, int d) {
   const int row = blockIdx.y;
@@ -169,6 +234,25 @@ extern "C" int nqt_fused_add_rmsnorm(void* x, void* residual, const void* weight
   else
     return NQT_ERR_UNSUPPORTED;
   return check_launch("fused_add_rmsnorm");
+}
+
+extern "C" int nqt_fused_add_rmsnorm_fp8(void* x, void* residual, const void* weight, int rows, int hidden, float eps,
+                                         void* q, int64_t ldq, float* scale, int64_t ld_scale, int write_x, int dtype,
+                                         void* stream) {
+  if (!x || !residual || !weight || !q || !scale || rows < 0 || hidden < 128 || hidden % 128 || x == residual)
+    return NQT_ERR_ARG;
+  if (dtype != NQT_BF16) return NQT_ERR_UNSUPPORTED;
+  if (hidden > kNormThreads * 8 * kMaxVec) return NQT_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(residual) || !aligned16(weight)) return NQT_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(q) & 7) || ldq % 8 || ldq < hidden || ld_scale < rows ||
+      (reinterpret_cast<uintptr_t>(scale) & 3))
+    return NQT_ERR_ARG;
+  if (rows == 0) return NQT_OK;
+  add_rmsnorm_fp8_kernel<<<rows, kNormThreads, 0, as_stream(stream)>>>(
+      static_cast<__nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(residual),
+      static_cast<const __nv_bfloat16*>(weight), hidden, eps, static_cast<uint8_t*>(q), ldq, scale, ld_scale,
+      write_x ? 1 : 0);
+  return check_launch("fused_add_rmsnorm_fp8");
 }
 
 extern "C" int nqt_silu_and_mul(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride, int rows,

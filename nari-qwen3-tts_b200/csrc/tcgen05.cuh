@@ -1,13 +1,13 @@
 // Fifth-generation tensor core (tcgen05) and Tensor Memory helpers, sm_100a.
 //
 // Inline PTX for: TMEM allocation, single-thread tcgen05.mma (kind::f16,
-// B from a shared memory descriptor, A from a descriptor or from TMEM,
-// fp32 accumulator in TMEM),
+// B from a shared memory descriptor, A from a descriptor or from TMEM;
+// kind::f8f6f4 with both operands from descriptors; fp32 accumulator in TMEM),
 // tcgen05.commit to an mbarrier, warp-collective 32x32b TMEM loads/stores
 // and the tcgen05 thread-sync fences; plus the 64-bit shared-memory matrix
 // descriptor and the 32-bit instruction descriptor encodings (PTX ISA,
 // "Tensor Core 5th Generation": matrix descriptors and instruction
-// descriptor for .kind::f16).
+// descriptors for .kind::f16 and .kind::f8f6f4).
 #pragma once
 
 #include "common.cuh"
@@ -59,6 +59,17 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc] with 8-bit operands (kind::f8f6f4): M x N x 32 per instruction.
+__device__ __forceinline__ void mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -118,6 +129,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n, bool a_mn_ma
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(a_mn_major) << 15) |
          (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Instruction descriptor, kind::f8f6f4 with e4m3 A and B (format code 0 in bits 7-9 and 10-12), fp32
+// accumulate, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
+  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 }  // namespace tc

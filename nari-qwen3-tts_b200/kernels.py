@@ -8,6 +8,8 @@ stream.  There is no CPU path: non-CUDA tensors are rejected.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -289,6 +291,7 @@ def cp_decode_attention_(
 
 
 __all__ = [
+    "Fp8BlockWeight",
     "PackedWeight",
     "clear_status",
     "cp_decode_attention_",
@@ -296,9 +299,14 @@ __all__ = [
     "device_status",
     "paired_qk_norm_rope_",
     "paired_qk_norm_rope_dense_cache_",
+    "fp8_gemm_workspace",
+    "fp8_quantize_rows",
     "fused_add_rmsnorm_",
+    "fused_add_rmsnorm_fp8_",
     "linear",
+    "linear_fp8",
     "paired_qk_norm_rope_paged_cache_",
+    "quantize_fp8_weight_blocks",
     "read_status",
     "rmsnorm",
     "silu_and_mul",
@@ -397,4 +405,142 @@ def linear(x: torch.Tensor, weight: PackedWeight, bias: torch.Tensor | None = No
         raise ValueError("linear bias must be contiguous bf16 [n]")
     call("nqt_gemm_bf16", ptr(x), x.stride(0), ptr(weight.data), ptr(out), out.stride(0), ptr(bias),
          m, weight.n, weight.k, epilogue, int(split), ptr(device_status(x.device)), _lib.stream_handle(x.device))
+    return out
+
+
+# ---------------------------------------------------------------- FP8 block-scaled gate/up
+def quantize_fp8_weight_blocks(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Quantise a row-major bf16 matrix into 128 x 128 e4m3 blocks with power-of-two scales, on the GPU
+    (model/layers.py:11-25: s = 2^ceil(log2(max(amax, 1e-4) / 448)), q = e4m3(w / s)).  Returns
+    (q [n, k] float8_e4m3fn, scales [n / 128, k / 128] float32), the reference's layouts."""
+
+    if weight.ndim != 2 or not weight.is_contiguous():
+        raise ValueError("FP8 block quantization requires a contiguous matrix")
+    rows, columns = weight.shape
+    if rows % 128 or columns % 128:
+        raise ValueError(
+            f"FP8 block quantization requires dimensions divisible by 128, got {tuple(weight.shape)}")
+    if weight.dtype != torch.bfloat16:
+        raise TypeError("FP8 block quantization takes a bf16 weight")
+    q = torch.empty((rows, columns), dtype=torch.float8_e4m3fn, device=weight.device)
+    scales = torch.empty((rows // 128, columns // 128), dtype=torch.float32, device=weight.device)
+    call("nqt_fp8_quantize_weight_blocks", ptr(weight), weight.stride(0), rows, columns, ptr(q), q.stride(0),
+         ptr(scales), _lib.stream_handle(weight.device))
+    return q, scales
+
+
+def fp8_quantize_rows(x: torch.Tensor, *, out: torch.Tensor | None = None,
+                      scale: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per token, per 128-element block: f = 448 / amax (1 when amax = 0), q = e4m3(x * f), scale 1 / f - the
+    bf16-input rule of the reference's FP8 gate/up GEMM (model/layers.py:242-256).  Returns (q [m, k]
+    float8_e4m3fn, scale [k / 128, m] float32: a block's tokens contiguous)."""
+
+    if x.dim() != 2 or x.dtype != torch.bfloat16 or x.stride(1) != 1:
+        raise ValueError("fp8_quantize_rows takes bf16 [m, k] with unit stride along k")
+    m, k = x.shape
+    if k % 128:
+        raise ValueError("fp8_quantize_rows needs k % 128 == 0")
+    if out is None:
+        out = torch.empty((m, k), dtype=torch.float8_e4m3fn, device=x.device)
+    if scale is None:
+        scale = torch.empty((k // 128, m), dtype=torch.float32, device=x.device)
+    if out.shape != (m, k) or out.dtype != torch.float8_e4m3fn or out.stride(1) != 1:
+        raise ValueError("fp8_quantize_rows output must be float8_e4m3fn [m, k] with unit column stride")
+    if scale.dim() != 2 or scale.shape[0] != k // 128 or scale.shape[1] < m or scale.stride(1) != 1 \
+            or scale.dtype != torch.float32:
+        raise ValueError("fp8_quantize_rows scale must be float32 [k / 128, >= m] with unit column stride")
+    call("nqt_fp8_quantize_rows", ptr(x), x.stride(0), m, k, ptr(out), out.stride(0), ptr(scale), scale.stride(0),
+         _lib.stream_handle(x.device))
+    return out, scale
+
+
+def fused_add_rmsnorm_fp8_(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                           q: torch.Tensor, scale: torch.Tensor, *, write_x: bool = False) -> None:
+    """residual <- x + residual; the normed row rmsnorm(residual) * weight (bf16) is quantised into q / scale
+    by the fp8_quantize_rows rule (and written to x when ``write_x``): the post-attention norm feeding the
+    FP8 gate/up GEMM."""
+
+    if not (x.is_contiguous() and residual.is_contiguous()) or x.shape != residual.shape or x.dim() != 2:
+        raise ValueError("fused_add_rmsnorm_fp8 needs contiguous [rows, hidden] tensors of one shape")
+    rows, hidden = x.shape
+    if q.shape != (rows, hidden) or q.dtype != torch.float8_e4m3fn or q.stride(1) != 1:
+        raise ValueError("fused_add_rmsnorm_fp8 q must be float8_e4m3fn [rows, hidden]")
+    if scale.dtype != torch.float32 or scale.dim() != 2 or scale.shape[0] != hidden // 128 or \
+            scale.shape[1] < rows or scale.stride(1) != 1:
+        raise ValueError("fused_add_rmsnorm_fp8 scale must be float32 [hidden / 128, >= rows]")
+    call("nqt_fused_add_rmsnorm_fp8", ptr(x), ptr(residual), ptr(weight), rows, hidden, float(eps), ptr(q),
+         q.stride(0), ptr(scale), scale.stride(0), 1 if write_x else 0, _lib.dtype_code(x.dtype),
+         _lib.stream_handle(x.device))
+
+
+class Fp8BlockWeight:
+    """A bf16 weight [n, k] quantised once (quantize_fp8_weight_blocks) and packed for nqt_gemm_fp8.
+    ``gate_up`` interleaves the gate and up halves in 64-row blocks for the SwiGLU epilogue.  Keeps the
+    reference-layout ``q`` and ``scale`` (the GEMM reads ``scale`` directly)."""
+
+    def __init__(self, weight: torch.Tensor, *, gate_up: bool = False) -> None:
+        n, k = weight.shape
+        if gate_up and n % 256:
+            raise ValueError("a gate_up weight needs n % 256 == 0")
+        self.n, self.k, self.gate_up = n, k, gate_up
+        self.q, self.scale = quantize_fp8_weight_blocks(weight)
+        self.data = torch.empty(n * k, dtype=torch.uint8, device=weight.device)
+        call("nqt_gemm_fp8_pack_weight", ptr(self.q), self.q.stride(0), n, k, 1 if gate_up else 0, ptr(self.data),
+             _lib.stream_handle(weight.device))
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return (self.n, self.k)
+
+
+_FP8_WORKSPACE: dict[tuple[int, int, int, int, int], torch.Tensor] = {}
+
+
+def fp8_gemm_workspace(device: torch.device, m: int, n: int, k: int, split: int = 0) -> torch.Tensor | None:
+    """The split-K workspace nqt_gemm_fp8 needs for this shape (None when it needs none): one zeroed buffer
+    per (device, shape), because a workspace's tickets are laid out for one launch shape (another shape's
+    partials would land on them).  Call it once outside graph capture for every shape a captured step uses;
+    a first call inside capture would allocate."""
+
+    nbytes = ctypes.c_int64(0)
+    call("nqt_gemm_fp8_workspace_bytes", m, n, k, int(split), ctypes.addressof(nbytes))
+    if nbytes.value == 0:
+        return None
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (index, m, n, k, int(split))
+    ws = _FP8_WORKSPACE.get(key)
+    if ws is None:
+        ws = torch.zeros(nbytes.value, dtype=torch.uint8, device=torch.device("cuda", index))
+        _FP8_WORKSPACE[key] = ws
+    return ws
+
+
+def linear_fp8(xq: torch.Tensor, xscale: torch.Tensor, weight: Fp8BlockWeight, *, out: torch.Tensor | None = None,
+               split: int = 0, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Block-scaled FP8 product Y = sum_b (Xq_b . Wq_b^T) * xscale[b, t] * wscale[row / 128, b] on the tcgen05
+    weight-streaming GEMM (the reference's FP8 gate/up, model/layers.py:242-256); a ``gate_up`` weight gives
+    silu(gate) * up, [m, n / 2].  ``split``: bits 0-7 CTAs sharing each tile's K (0 automatic), bits 8-11 K
+    blocks per copy stage (0 automatic).  ``workspace``: the split-K buffer (fp8_gemm_workspace by default;
+    one launch at a time per buffer)."""
+
+    if not isinstance(weight, Fp8BlockWeight):
+        raise TypeError("linear_fp8 takes an Fp8BlockWeight")
+    if xq.dim() != 2 or xq.shape[1] != weight.k or xq.dtype != torch.float8_e4m3fn or xq.stride(1) != 1:
+        raise ValueError("linear_fp8 needs xq float8_e4m3fn [m, k] matching the weight")
+    m = xq.shape[0]
+    if xscale.dtype != torch.float32 or xscale.dim() != 2 or xscale.shape[0] != weight.k // 128 or \
+            xscale.shape[1] < m or xscale.stride(1) != 1:
+        raise ValueError("linear_fp8 xscale must be float32 [k / 128, >= m]")
+    cols = weight.n // 2 if weight.gate_up else weight.n
+    if out is None:
+        out = torch.empty((m, cols), dtype=torch.bfloat16, device=xq.device)
+    elif out.shape != (m, cols) or out.dtype != torch.bfloat16 or out.stride(1) != 1:
+        raise ValueError("linear_fp8 output must be bf16 [m, n] with unit column stride")
+    epilogue = GEMM_SILU_MUL if weight.gate_up else GEMM_PLAIN
+    if workspace is None:
+        workspace = fp8_gemm_workspace(xq.device, m, weight.n, weight.k, split)
+    call("nqt_gemm_fp8", ptr(xq), xq.stride(0), ptr(xscale), xscale.stride(0), ptr(weight.data), ptr(weight.scale),
+         ptr(out), out.stride(0), m, weight.n, weight.k, epilogue, 1 if weight.gate_up else 0, int(split),
+         ptr(workspace), 0 if workspace is None else workspace.numel(), ptr(device_status(xq.device)),
+         _lib.stream_handle(xq.device))
     return out

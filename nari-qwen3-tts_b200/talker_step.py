@@ -10,7 +10,8 @@ with the layer loop of model/components.py:74-90):
         QKV projection (cuBLAS)
         attend: QK RMSNorm + RoPE + paged K/V write, paged decode (talker_kv.py)
         O projection (cuBLAS), fused residual add + RMSNorm
-        gate/up (cuBLAS), SiLU * up, down (cuBLAS), fused add + RMSNorm (next norm)
+        gate/up (FP8 GEMM with SwiGLU fused, or cuBLAS + SiLU * up), down (cuBLAS),
+        fused add + RMSNorm (next norm)
     codec head (cuBLAS), suppress mask, fused sampler with the seen-mask update,
     device completion rule (terminal flags, step and RNG offset += 512), commit
 
@@ -23,7 +24,11 @@ There is no host round trip inside the step.  ``step()`` is the host-facing
 call: it copies the step's inputs from pinned host memory, replays the
 graph and returns the sampled tokens to the host.
 
-Weights are random (bf16); GEMMs are plain library calls (torch -> cuBLAS).
+Weights are random (bf16).  The gate/up projection takes the reference's
+production FP8 path by default (``gate_up="fp8"``: 128 x 128 e4m3 weight
+blocks, the post-attention norm writing e4m3 activation blocks, the
+block-scaled tcgen05 GEMM with SwiGLU fused); ``gate_up="bf16"`` keeps it in
+bf16.  The other projections are library calls (torch -> cuBLAS).
 """
 
 from __future__ import annotations
@@ -112,13 +117,34 @@ def _kv_pool(shape: TalkerShape, total_pages: int, page_size: int, device, gener
     return storage
 
 
-def _mlp_block(weights: TalkerWeights, shape: TalkerShape, layer: int, o: torch.Tensor, residual: torch.Tensor,
-               act: torch.Tensor) -> torch.Tensor:
-    """residual += o; MLP(norm(residual)); residual += mlp; returns the next layer's normed input."""
+class GateUpFp8:
+    """The reference's production gate/up for a step's rows (executor/build.py:73 requires it on every talker
+    layer; model/layers.py:195-270): the weights quantised once into 128 x 128 e4m3 blocks, the post-attention
+    add + RMSNorm writing e4m3 rows with per-128 scales, and the block-scaled tcgen05 GEMM with SwiGLU fused."""
 
-    kernels.fused_add_rmsnorm_(o, residual, weights.ln_post[layer], shape.eps)
-    gate_up = F.linear(o, weights.w_gate_up[layer])
-    kernels.silu_and_mul(gate_up, out=act)
+    def __init__(self, weights: TalkerWeights, shape: TalkerShape, rows: int, device: torch.device) -> None:
+        self.weights = [kernels.Fp8BlockWeight(w, gate_up=True) for w in weights.w_gate_up]
+        self.q = torch.empty(rows, shape.hidden, dtype=torch.float8_e4m3fn, device=device)
+        self.scale = torch.empty(shape.hidden // 128, rows, dtype=torch.float32, device=device)
+        # the split-K workspace is made here, outside any graph capture
+        self.workspace = kernels.fp8_gemm_workspace(device, rows, 2 * shape.ffn, shape.hidden)
+
+    def bytes(self) -> int:
+        return sum(w.data.numel() + w.scale.numel() * 4 for w in self.weights)
+
+
+def _mlp_block(weights: TalkerWeights, shape: TalkerShape, layer: int, o: torch.Tensor, residual: torch.Tensor,
+               act: torch.Tensor, fp8: GateUpFp8 | None = None) -> torch.Tensor:
+    """residual += o; MLP(norm(residual)); residual += mlp; returns the next layer's normed input.  With ``fp8``
+    the gate/up projection takes the reference's FP8 path."""
+
+    if fp8 is None:
+        kernels.fused_add_rmsnorm_(o, residual, weights.ln_post[layer], shape.eps)
+        gate_up = F.linear(o, weights.w_gate_up[layer])
+        kernels.silu_and_mul(gate_up, out=act)
+    else:
+        kernels.fused_add_rmsnorm_fp8_(o, residual, weights.ln_post[layer], shape.eps, fp8.q, fp8.scale)
+        kernels.linear_fp8(fp8.q, fp8.scale, fp8.weights[layer], out=act, workspace=fp8.workspace)
     m = F.linear(act, weights.w_down[layer])
     nxt = weights.ln_final if layer + 1 == shape.num_layers else weights.ln_in[layer + 1]
     kernels.fused_add_rmsnorm_(m, residual, nxt, shape.eps)
@@ -137,8 +163,12 @@ class TalkerDecodeStep:
         device: torch.device | str = "cuda",
         seed: int = 0,
         publish: bool = True,
+        gate_up: str = "fp8",
     ) -> None:
+        if gate_up not in ("fp8", "bf16"):
+            raise ValueError("gate_up is 'fp8' (the reference's production path) or 'bf16'")
         self.shape = s = shape
+        self.gate_up = gate_up
         # publish=False discards each step's reservation after the step, so every
         # step sees the same context lengths (a stationary benchmark workload)
         self.publish = publish
@@ -167,6 +197,7 @@ class TalkerDecodeStep:
         self._x = torch.empty(batch, s.hidden, dtype=bf16, device=dev)
         self._residual = torch.empty(batch, s.hidden, dtype=bf16, device=dev)
         self._act = torch.empty(batch, s.ffn, dtype=bf16, device=dev)
+        self.fp8 = GateUpFp8(self.weights, s, batch, dev) if gate_up == "fp8" else None
         self.graph: torch.cuda.CUDAGraph | None = None
         self.contexts: list[int] = []
         # parity hook: Exp(1) noise [batch, vocab] for the sampler's noise entry instead of the Philox draw
@@ -219,10 +250,16 @@ class TalkerDecodeStep:
         self.seen.scatter_(1, ids.to(self.device), True)
 
     # ---------------------------------------------------------------- step body
+    def _mlp_rows(self) -> tuple:
+        """The layer's FP8 MLP input (e4m3 rows, scales) for a parity trace; empty on the bf16 path."""
+
+        return () if self.fp8 is None else (self.fp8.q.clone(), self.fp8.scale.clone())
+
     def forward(self, trace: list | None = None) -> torch.Tensor:
         """The step body (what capture() records).  ``trace``, for parity
         tests of an eager step: receives (normed input, residual) before the
-        first layer and after every layer, then the logits."""
+        first layer and after every layer - plus, on the FP8 path, the layer's
+        e4m3 MLP input rows and their scales - then the logits."""
 
         s = self.shape
         b = self.binding
@@ -245,9 +282,9 @@ class TalkerDecodeStep:
             v = qkv[:, (hq + hkv) * d:].view(rows, hkv, d)
             attn = b.attend(w.attn[layer], q, k, v)
             o = F.linear(attn.view(rows, hq * d), w.w_o[layer])
-            x = _mlp_block(w, s, layer, o, residual, self._act)
+            x = _mlp_block(w, s, layer, o, residual, self._act, self.fp8)
             if trace is not None:
-                trace.append((x.clone(), residual.clone()))
+                trace.append((x.clone(), residual.clone()) + self._mlp_rows())
         self.last_hidden = x  # the final normed hidden state (the code predictor's input)
         logits = ctl.mask_logits(F.linear(x, w.w_head))
         if trace is not None:
@@ -304,7 +341,12 @@ class TalkerDecodeStep:
         return kv + qo
 
     def weight_bytes(self) -> int:
-        return self.weights.bytes()
+        """Weight bytes one step streams (the FP8 gate/up in place of its bf16 copy)."""
+
+        total = self.weights.bytes()
+        if self.fp8 is not None:
+            total += self.fp8.bytes() - sum(w.numel() * w.element_size() for w in self.weights.w_gate_up)
+        return total
 
 
 class TalkerMixedStep:
@@ -326,8 +368,11 @@ class TalkerMixedStep:
 
     def __init__(self, *, shape: TalkerShape = TalkerShape(), chunks: list[int], decode_contexts: list[int],
                  churn_rows: int = 24, total_pages: int, page_size: int = 16, device: torch.device | str = "cuda",
-                 seed: int = 0) -> None:
+                 seed: int = 0, gate_up: str = "fp8") -> None:
+        if gate_up not in ("fp8", "bf16"):
+            raise ValueError("gate_up is 'fp8' (the reference's production path) or 'bf16'")
         self.shape = s = shape
+        self.gate_up = gate_up
         self.device = dev = torch.device(device)
         self.page_size = P = page_size
         self.chunks = list(chunks)
@@ -368,6 +413,7 @@ class TalkerMixedStep:
         self._residual = torch.empty(self.tokens, s.hidden, dtype=bf16, device=dev)
         self._attn = torch.empty(self.tokens, s.num_heads * s.head_dim, dtype=bf16, device=dev)
         self._act = torch.empty(self.tokens, s.ffn, dtype=bf16, device=dev)
+        self.fp8 = GateUpFp8(self.weights, s, self.tokens, dev) if gate_up == "fp8" else None
         ends = torch.tensor(chunks).cumsum(0) - 1
         self._sample_rows = torch.cat([ends, self.t_pre + torch.arange(self.n_dec)]).to(dev)
         n = self.rows
@@ -416,6 +462,8 @@ class TalkerMixedStep:
         self.seen.zero_()
         self.seen.scatter_(1, ids.to(self.device), True)
 
+    _mlp_rows = TalkerDecodeStep._mlp_rows
+
     def forward(self, trace: list | None = None) -> torch.Tensor:
         """The step body; ``trace`` as in TalkerDecodeStep.forward (over all
         packed tokens, prefill chunks first)."""
@@ -451,9 +499,9 @@ class TalkerMixedStep:
                                self.dec_b.paged_kv_last_page_len, self.dec_b.decode_workspace, batch_capacity=nd,
                                out=attn[tp:], plan=False)
             o = F.linear(self._attn, w.w_o[layer])
-            x = _mlp_block(w, s, layer, o, residual, self._act)
+            x = _mlp_block(w, s, layer, o, residual, self._act, self.fp8)
             if trace is not None:
-                trace.append((x.clone(), residual.clone()))
+                trace.append((x.clone(), residual.clone()) + self._mlp_rows())
         logits = ctl.mask_logits(F.linear(x.index_select(0, self._sample_rows), w.w_head))
         if trace is not None:
             trace.append(logits.clone())

@@ -36,6 +36,7 @@ import time
 import torch
 
 from . import attention as oatt
+from . import fp8 as ofp8
 from . import planner as oplan
 from . import sampler as osamp
 
@@ -61,7 +62,8 @@ def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: f
 
 
 def layer_forward(x, residual, *, w_qkv, w_o, w_gate_up, w_down, ln_post, ln_next, q_norm, k_norm, eps, theta,
-                  heads, kv_heads, head_dim, cache, meta, prefill_rows=0):
+                  heads, kv_heads, head_dim, cache, meta, prefill_rows=0, gate_up_fp8=False, fp8_rows=None,
+                  probe=None):
     """One decoder layer, teacher-forced.
 
     x: the layer's normed input, residual: the residual stream (both [T, hidden],
@@ -70,6 +72,10 @@ def layer_forward(x, residual, *, w_qkv, w_o, w_gate_up, w_down, ln_post, ln_nex
     group ``pos, wp, wo, indptr, indices, last``; with ``prefill_rows`` > 0 the
     first ``prefill_rows`` tokens form a prefill group described by
     ``pre_*`` keys (``pre_qo_indptr`` included) and the rest the decode group.
+    ``gate_up_fp8``: the gate/up projection takes the reference's FP8 path (128 x 128 weight blocks, per-token
+    128-element activation blocks, oracle/fp8.py) instead of bf16; ``fp8_rows`` = (e4m3 rows, scales) replaces
+    the quantised MLP input (teacher forcing at the quantisation step).  ``probe``, a dict, receives the MLP
+    input ("mlp_in", bf16 values).
     Returns (next normed input, residual), bf16 values in fp32 tensors.
     """
 
@@ -97,9 +103,16 @@ def layer_forward(x, residual, *, w_qkv, w_o, w_gate_up, w_down, ln_post, ln_nex
             attn[lo:hi] = oatt.paged_decode(qs.float(), cache, meta["indptr"], meta["indices"], meta["last"])
     o = _round(_round(attn).reshape(t, h * d) @ w_o.float().T)
     x2, residual = add_rmsnorm(o, residual, ln_post, eps)
-    gu = _round(x2 @ w_gate_up.float().T)
-    ffn = gu.shape[1] // 2
-    act = _round(torch.nn.functional.silu(gu[:, :ffn]) * gu[:, ffn:])
+    if probe is not None:
+        probe["mlp_in"] = x2
+    if gate_up_fp8:
+        xq, xs = fp8_rows if fp8_rows is not None else ofp8.quantize_rows(x2.to(BF16))
+        wq, ws = ofp8.quantize_weight_blocks(w_gate_up.to(BF16))
+        act = ofp8.swiglu(ofp8.gemm_blockscaled(xq, xs, wq, ws)).float()
+    else:
+        gu = _round(x2 @ w_gate_up.float().T)
+        ffn = gu.shape[1] // 2
+        act = _round(torch.nn.functional.silu(gu[:, :ffn]) * gu[:, ffn:])
     m = _round(act @ w_down.float().T)
     return add_rmsnorm(m, residual, ln_next, eps)
 

@@ -20,6 +20,10 @@ and outputs as small torch files next to this script:
                 prepare_capture, :485-533), recorded by a stand-in binding,
                 so the drop-in binding can be replayed against exactly
                 those calls without the reference installed.
+  fp8.pt        quantize_fp8_weight_blocks (model/layers.py:11-25) on a
+                seeded bf16 weight whose 128 x 128 blocks cover a zero block,
+                an amax below the 1e-4 clamp, amax exactly 448 * 2^k, huge and
+                subnormal magnitudes and ordinary N(0, 1) data.
   attention.pt  RMSNorm.forward + Qwen3TTSCodePredictor._apply_rope
                 (model/layers.py:103-115, model/components.py:214-233) on
                 bf16 heads, and _depth_attention (components.py:236-252) on
@@ -47,7 +51,7 @@ def _import_reference():
     from nari_qwen3_tts.contract import TalkerDecodeCaptureKey, TalkerPrefillCaptureKey
     from nari_qwen3_tts.executor.talker_kv import PagedTalkerKV
     from nari_qwen3_tts.model.components import Qwen3TTSCodePredictor
-    from nari_qwen3_tts.model.layers import RMSNorm
+    from nari_qwen3_tts.model.layers import RMSNorm, quantize_fp8_weight_blocks
     from nari_qwen3_tts.model.sampling import sample_logits_stateless
 
     return {
@@ -56,6 +60,7 @@ def _import_reference():
         "PagedTalkerKV": PagedTalkerKV,
         "CP": Qwen3TTSCodePredictor,
         "RMSNorm": RMSNorm,
+        "quantize_fp8": quantize_fp8_weight_blocks,
         "sample": sample_logits_stateless,
     }
 
@@ -345,14 +350,43 @@ def make_binding(ref) -> dict:
     return {"factories": factories, "calls": calls, "metadata_fields": list(_META_FIELDS)}
 
 
+def make_fp8(ref) -> dict:
+    """A [256, 768] bf16 weight: six 128 x 128 blocks per block row, each a different regime."""
+
+    g = torch.Generator().manual_seed(11)
+    w = torch.randn(256, 768, generator=g)
+    blocks = w.view(2, 128, 6, 128)
+    blocks[0, :, 0] = 0.0                                   # all zero: amax clamped to 1e-4
+    blocks[0, :, 1] *= 2e-5                                 # amax below the clamp
+    blocks[0, :, 2] = blocks[0, :, 2].clamp(-50, 50)        # amax exactly 448 * 2^-3 (a power-of-two scale)
+    blocks[0, 7, 2, 9] = -56.0
+    blocks[0, :, 3] *= 1e30                                 # huge magnitudes
+    blocks[0, :, 4] *= 1e-38                                # bf16 subnormals: quantise to zero
+    blocks[0, :, 5] = blocks[0, :, 5].clamp(-400, 400)      # amax exactly 448
+    blocks[0, 100, 5, 3] = 448.0
+    blocks[1] *= torch.logspace(-3, 3, 6).view(1, 6, 1)    # ordinary data over six decades
+    weight = w.to(torch.bfloat16).contiguous()
+    q, scales = ref["quantize_fp8"](weight)
+    return {"weight": weight, "q": q.view(torch.uint8).clone(), "scales": scales.clone()}
+
+
+MAKERS = {
+    "sampler": make_sampler,
+    "planner": make_planner,
+    "attention": make_attention,
+    "binding": make_binding,
+    "fp8": make_fp8,
+}
+
+
 def main() -> None:
+    """Writes every fixture, or only those named on the command line (e.g. ``make_golden.py fp8``)."""
+
     ref = _import_reference()
-    torch.save(make_sampler(ref), HERE / "sampler.pt")
-    torch.save(make_planner(ref), HERE / "planner.pt")
-    torch.save(make_attention(ref), HERE / "attention.pt")
-    torch.save(make_binding(ref), HERE / "binding.pt")
-    for name in ("sampler.pt", "planner.pt", "attention.pt", "binding.pt"):
-        print(name, (HERE / name).stat().st_size, "bytes")
+    names = sys.argv[1:] or list(MAKERS)
+    for name in names:
+        torch.save(MAKERS[name](ref), HERE / f"{name}.pt")
+        print(f"{name}.pt", (HERE / f"{name}.pt").stat().st_size, "bytes")
 
 
 if __name__ == "__main__":
