@@ -66,6 +66,10 @@ def parse() -> argparse.Namespace:
     p.add_argument("--serve-seconds", type=float, default=10.0, help="config 5: arrival window per GPU (s)")
     p.add_argument("--serve-rps", type=float, default=20.0, help="config 5: Poisson arrival rate per GPU")
     p.add_argument("--layers", type=int, default=28, help="decoder layers (28 = BASELINE config 2)")
+    p.add_argument("--gate-up", choices=("fp8", "bf16"), default=None,
+                   help="talker gate/up: fp8 = the reference's production path (128x128 e4m3 weight blocks, "
+                        "per-token 1x128 activation blocks); bf16 = unquantised.  Default: fp8 for the decode "
+                        "step, bf16 for the mixed batch (prefill-scale M)")
     p.add_argument("--pool-tokens", type=int, default=POOL_TOKENS)
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -242,7 +246,9 @@ def run_reference(args, world, rank):
         "data": "synthetic (random-init weights, N(0,1) KV, seeded ragged contexts)",
         "config": {"workload": "BASELINE config 2: talker decode step, B=64, ctx U[64,2048], 28 layers, "
                                "P=16, 512k-token pool", "global_batch": BATCH, "seq_len": CTX_HI,
-                   "parallelism": "cpu (one host process at every N)"},
+                   "parallelism": "cpu (one host process at every N)",
+                   "gate_up": "bf16: the reference quantises gate/up to FP8 only on a CUDA device "
+                              "(model/layers.py:225-237), so its CPU path keeps bf16"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -291,7 +297,8 @@ def run_mixed(args, world, rank, local, emit: bool = True) -> dict:
     shape = talker_step.TalkerShape(num_layers=args.layers)
     pool_tokens = max(args.pool_tokens, sum(decode_ctx) + sum(chunks) + 64 * 1024)
     step = talker_step.TalkerMixedStep(shape=shape, chunks=chunks, decode_contexts=decode_ctx, churn_rows=24,
-                                       total_pages=pool_tokens // 16, page_size=16, device=dev, seed=rank)
+                                       total_pages=pool_tokens // 16, page_size=16, device=dev, seed=rank,
+                                       gate_up=args.gate_up or "bf16")
     step.admit(scatter_seed=rank)
     step.capture(warmup=2)
     for _ in range(args.warmup):
@@ -355,6 +362,7 @@ def run_mixed(args, world, rank, local, emit: bool = True) -> dict:
             "seq_len": 4096,
             "parallelism": f"dp{world} (request-sharded, no collective)",
             "l2": "inputs larger than L2: ~57 GB of decode KV read per step",
+            "gate_up": GATE_UP_NOTE[args.gate_up or "bf16"],
         },
         "decode_seq_steps_per_s": world * step.n_dec / (ms / 1e3),
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak_tflops(), "unit": "TFLOP/s",
@@ -740,6 +748,13 @@ def run_serve(args, world, rank, local) -> None:
         dist.destroy_process_group()
 
 
+GATE_UP_NOTE = {
+    "fp8": "fp8 e4m3: 128x128 weight blocks with power-of-two scales, per-token 1x128 activation blocks, "
+           "fp32 accumulation (the reference's production talker path, executor/build.py:73)",
+    "bf16": "bf16 (unquantised)",
+}
+
+
 def main() -> None:
     args = parse()
     world, rank, local = dist_setup(args)
@@ -769,7 +784,7 @@ def main() -> None:
     pages = args.pool_tokens // 16
     step = talker_step.TalkerDecodeStep(shape=shape, batch=BATCH, total_pages=pages, page_size=16,
                                         max_pages_per_seq=(CTX_HI + 1024) // 16, device=dev, seed=rank,
-                                        publish=args.grow)
+                                        publish=args.grow, gate_up=args.gate_up or "fp8")
     contexts = contexts_for(rank)
     step.admit(contexts, scatter_seed=rank)
     lib_mod.reset_launch_count()
@@ -879,6 +894,7 @@ def main() -> None:
             "seq_len": CTX_HI,
             "parallelism": f"dp{world} (request-sharded, no collective)",
             "l2": "inputs larger than L2: ~8.5 GB of KV read per step",
+            "gate_up": GATE_UP_NOTE[args.gate_up or "fp8"],
             "contexts": "held at the sampled lengths (each step's reservation is discarded)" if not args.grow
             else "growing by one token per step (published)",
         },

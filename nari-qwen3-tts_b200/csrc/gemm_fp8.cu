@@ -35,12 +35,14 @@
 // then hand the buffer back to the MMA issuer, so the promotion overlaps the
 // weight stream.  The scale products are staged in shared memory once per CTA.
 //
-// Split-K sum (S > 1): every CTA writes its fp32 partial [tokens][128 rows] to a
-// global workspace (L2-resident) and counts in on the tile's ticket (one thread
-// fences after a CTA barrier); the CTA that completes the ticket returns it to
-// zero, brings all S partials into its drained stage ring with bulk copies and
-// adds them in rank order (so the result does not depend on which CTA finished
-// last), then runs the epilogue.  No CTA waits for another.
+// Split-K sum (S > 1): every CTA first takes its tile's ticket.  The others write
+// their fp32 partial [tokens][128 rows] to a global workspace (L2-resident) and
+// count it in on the tile's `written` counter; the CTA that completes the ticket
+// parks its own partial in shared memory, waits (bounded) until the others have
+// written - they all hold tickets already, so they are resident and finish
+// unconditionally - returns both counters to zero, brings their partials into its
+// drained stage ring with bulk copies and adds all S in rank order (so the result
+// does not depend on which CTA finished last), then runs the epilogue.
 // Epilogues: plain (Y = bf16) and SwiGLU, Y = silu(bf16 g) * bf16 u (the unfused
 // GEMM followed by silu_and_mul), on gate/up rows packed in 32-row groups
 // [gate 16 | up 16] (a tile holds gate and up rows 64 t .. 64 t + 63): lanes l and
@@ -87,7 +89,7 @@ struct Fp8Args {
   __nv_bfloat16* y;
   int64_t ldy;
   float* partials;   // [chunks][tiles][S][MP][128] (S > 1)
-  int32_t* tickets;  // [chunks][tiles] (S > 1), zero between launches
+  int32_t* tickets;  // [2][chunks][tiles] (S > 1): tickets, then written counters; zero between launches
   int32_t* status;
   int m, n, kbt;
   int epilogue, interleave;
@@ -98,10 +100,9 @@ struct Fp8Args {
 __host__ __device__ constexpr int x_bytes(int mp) { return mp * kBlockK; }
 // a stage: `group` W units [group][128 x 128 B] then their X slabs [group][mp x 128 B]
 __host__ __device__ constexpr int stage_bytes(int mp, int group) { return group * (kWBytes + x_bytes(mp)); }
-// the drained ring is reused by the split-K sum (one partial [mp][128] fp32 at least) and the SwiGLU
-// exchange ([2][mp / 2][64] fp32)
+// the drained ring is reused by the split-K sum: two partials [mp][128] fp32 at least (the own one and a copy)
 __host__ __device__ constexpr int ring_bytes(int mp, int group, int stages) {
-  return stages * stage_bytes(mp, group) > mp * 512 ? stages * stage_bytes(mp, group) : mp * 512;
+  return stages * stage_bytes(mp, group) > mp * 1024 ? stages * stage_bytes(mp, group) : mp * 1024;
 }
 // per-CTA scale products sx[b, t] * sw[half, b] as [2 halves][units][mp]
 __host__ __device__ constexpr int tables_bytes(int mp, int units) { return 2 * units * mp * 4; }
@@ -302,49 +303,77 @@ __global__ void __launch_bounds__(kThreads, MINB)
     }
     bool last = true;
     if (S > 1) {
-      // split K: partial to the workspace, count in on the tile's ticket; the CTA that completes it sums
+      // split K: take the tile's ticket first.  The CTA that completes it sums; the others write their partial
+      // to the workspace and count it in on the tile's `written` counter.  The summing CTA waits for that
+      // count only on CTAs that already hold a ticket (resident, and writing unconditionally), so the wait
+      // ends; it keeps its own partial in shared memory, off the global round trip.
       const int64_t slot = static_cast<int64_t>(blockIdx.z) * gridDim.x + tile;
+      const int64_t slots = static_cast<int64_t>(gridDim.z) * gridDim.x;
+      int32_t* ticket = a.tickets + slot;
+      int32_t* written = a.tickets + slots + slot;
       float* parts = a.partials + slot * S * MP * kTileN;
       constexpr uint32_t kPart = MP * kTileN * 4;  // bytes of one partial
-      const int per_round = ring_bytes(MP, G, ST) / static_cast<int>(kPart);  // partials the drained ring holds
-#pragma unroll
-      for (int e = 0; e < MP; ++e) __stcg(parts + (rank * MP + e) * kTileN + row, acc[e]);
-      epi_bar();  // the CTA's stores happen before thread 64's release below
-      if (threadIdx.x == 64) {
-        __threadfence();
-        const int old = atomicAdd(a.tickets + slot, 1);
-        const bool mine = old == S - 1;
-        if (mine) {
-          a.tickets[slot] = 0;  // every CTA of this tile has counted in: reset for the next launch
-          __threadfence();      // acquire the other CTAs' partials ...
-          fence_proxy_async_global();  // ... for the bulk copies below
-        }
-        *s_last = mine ? 1 : 0;
-      }
+      // the drained ring holds `cap` partials: the own one in the last slot, copies in the others
+      const int cap = ring_bytes(MP, G, ST) / static_cast<int>(kPart);
+      float* own = reinterpret_cast<float*>(smem + (cap - 1) * kPart);
+      if (threadIdx.x == 64) *s_last = atomicAdd(ticket, 1) == S - 1 ? 1 : 0;
       epi_bar();
       last = *s_last != 0;
-      if (last) {
-        // every partial, this CTA's own included, comes into the drained ring by bulk copies (`per_round` at
-        // a time) and is added in rank order: the sum does not depend on which CTA completed the ticket
+      if (!last) {
+#pragma unroll
+        for (int e = 0; e < MP; ++e) __stcg(parts + (rank * MP + e) * kTileN + row, acc[e]);
+        epi_bar();  // the CTA's stores happen before thread 64's release below
+        if (threadIdx.x == 64) {
+          __threadfence();
+          atomicAdd(written, 1);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < MP; ++e) own[e * kTileN + row] = acc[e];
+        if (threadIdx.x == 64) {
+          bool ready = false;
+          const uint64_t start = global_timer_ns();
+          while (true) {
+            if (ld_acquire_gpu(written) >= S - 1) {
+              ready = true;
+              break;
+            }
+            if (global_timer_ns() - start > kWaitLimitNs) break;
+          }
+          if (!ready) report(a.status, NQT_DEV_TIMEOUT);
+          *ticket = 0;  // every CTA of this tile has counted in on both: reset for the next launch
+          *written = 0;
+          fence_proxy_async_global();  // the acquired partials are read by the bulk copies below
+        }
+        // every partial is added in rank order (the own one from shared memory), `cap - 1` copies per
+        // round: the sum does not depend on which CTA completed the ticket
 #pragma unroll
         for (int e = 0; e < MP; ++e) acc[e] = 0.f;
+        const int per_round = cap - 1;
         int p = 0, round = 0;
         while (p < S) {
-          const int cnt = S - p < per_round ? S - p : per_round;
-          if (threadIdx.x == 64) {
-            mbar_arrive_expect_tx(sumbar, static_cast<uint32_t>(cnt) * kPart);
-            for (int j = 0; j < cnt; ++j)
-              bulk_load(smem + j * kPart, parts + static_cast<int64_t>(p + j) * MP * kTileN, kPart, sumbar);
+          // partials p .. q - 1 this round: up to per_round copies, the own one free
+          int q = p, copies = 0;
+          while (q < S && (q == rank || copies < per_round)) copies += q++ != rank ? 1 : 0;
+          if (copies > 0) {
+            epi_bar();  // (first round: the own partial is parked; later: the previous round is read)
+            if (threadIdx.x == 64) {
+              mbar_arrive_expect_tx(sumbar, static_cast<uint32_t>(copies) * kPart);
+              for (int r = p, j = 0; r < q; ++r)
+                if (r != rank) bulk_load(smem + (j++) * kPart, parts + static_cast<int64_t>(r) * MP * kTileN, kPart,
+                                         sumbar);
+            }
+          } else {
+            epi_bar();
           }
-          const bool got = mbar_wait(sumbar, round & 1, a.status);
-          for (int j = 0; j < cnt && got; ++j) {
-            const float* src = reinterpret_cast<const float*>(smem + j * kPart) + row;
+          const bool got = copies == 0 || mbar_wait(sumbar, round & 1, a.status);
+          for (int r = p, j = 0; r < q && got; ++r) {
+            const float* src = (r == rank ? own : reinterpret_cast<const float*>(smem + (j++) * kPart)) + row;
 #pragma unroll
             for (int e = 0; e < MP; ++e) acc[e] += src[e * kTileN];
           }
-          p += cnt;
-          ++round;
-          epi_bar();  // every thread has read this round before the next one lands
+          if (copies > 0) ++round;
+          p = q;
         }
       }
     }
@@ -553,7 +582,7 @@ int plan_fp8(int m, int n, int k, int split, Plan* pl) {
   const int floor = tmem_smem_floor(static_cast<int>(p.tmem_cols));
   if (p.smem < floor) p.smem = floor;
   if (p.smem > budget) return NQT_ERR_UNSUPPORTED;
-  p.ticket_bytes = S > 1 ? (base * 4 + 255) / 256 * 256 : 0;
+  p.ticket_bytes = S > 1 ? (2 * base * 4 + 255) / 256 * 256 : 0;  // tickets, then the written counters
   p.workspace_bytes = S > 1 ? p.ticket_bytes + base * S * p.mp * kTileN * 4 : 0;
   *pl = p;
   return NQT_OK;

@@ -24,11 +24,14 @@ There is no host round trip inside the step.  ``step()`` is the host-facing
 call: it copies the step's inputs from pinned host memory, replays the
 graph and returns the sampled tokens to the host.
 
-Weights are random (bf16).  The gate/up projection takes the reference's
-production FP8 path by default (``gate_up="fp8"``: 128 x 128 e4m3 weight
-blocks, the post-attention norm writing e4m3 activation blocks, the
+Weights are random (bf16).  The decode step's gate/up projection takes the
+reference's production FP8 path by default (``gate_up="fp8"``: 128 x 128 e4m3
+weight blocks, the post-attention norm writing e4m3 activation blocks, the
 block-scaled tcgen05 GEMM with SwiGLU fused); ``gate_up="bf16"`` keeps it in
-bf16.  The other projections are library calls (torch -> cuBLAS).
+bf16.  The mixed step defaults to bf16: its gate/up multiplies thousands of
+prefill tokens, where the FP8 kernel (built to stream weights for decode-sized
+batches) is slower than cuBLAS.  The other projections are library calls
+(torch -> cuBLAS), as in the reference.
 """
 
 from __future__ import annotations
@@ -368,7 +371,7 @@ class TalkerMixedStep:
 
     def __init__(self, *, shape: TalkerShape = TalkerShape(), chunks: list[int], decode_contexts: list[int],
                  churn_rows: int = 24, total_pages: int, page_size: int = 16, device: torch.device | str = "cuda",
-                 seed: int = 0, gate_up: str = "fp8") -> None:
+                 seed: int = 0, gate_up: str = "bf16") -> None:
         if gate_up not in ("fp8", "bf16"):
             raise ValueError("gate_up is 'fp8' (the reference's production path) or 'bf16'")
         self.shape = s = shape
