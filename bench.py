@@ -60,9 +60,10 @@ def parse() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=300)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("decode", "mixed", "cp", "sampler", "serve"), default="decode",
+    p.add_argument("--workload", choices=("decode", "mixed", "cp", "sampler", "serve", "gate_up"), default="decode",
                    help="decode = BASELINE config 2 (the headline); mixed = config 4 (prefill chunks + decode rows); "
-                        "cp = config 3; serve = config 5 (box serving simulation); sampler = the sampler roofline")
+                        "cp = config 3; serve = config 5 (box serving simulation); sampler = the sampler roofline; "
+                        "gate_up = the FP8 gate/up GEMM against cuBLAS bf16")
     p.add_argument("--serve-seconds", type=float, default=10.0, help="config 5: arrival window per GPU (s)")
     p.add_argument("--serve-rps", type=float, default=20.0, help="config 5: Poisson arrival rate per GPU")
     p.add_argument("--layers", type=int, default=28, help="decoder layers (28 = BASELINE config 2)")
@@ -589,6 +590,98 @@ class SamplerWorkload:
                 "peak_source": f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"}
 
 
+def run_gate_up(args, world, rank, local, emit: bool = True) -> dict:
+    """The talker's FP8 gate/up GEMM (the reference's production path) on its own: 28 layers of gate/up
+    weights (larger than L2) called in turn from one CUDA graph, B = 64 rows quantised by the activation rule,
+    SwiGLU fused; cuBLAS bf16 gate_up + silu_and_mul on the same weights timed beside it."""
+
+    from importlib import import_module
+
+    nqt = import_module("nari-qwen3-tts_b200")
+    lib_mod = import_module("nari-qwen3-tts_b200._lib")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    layers, rows, hidden, ffn = args.layers, BATCH, 2048, 6144
+    g = torch.Generator(device=dev).manual_seed(6000 + rank)
+    w16 = [(torch.randn(2 * ffn, hidden, generator=g, device=dev) * hidden ** -0.5).to(torch.bfloat16)
+           for _ in range(layers)]
+    w8 = [nqt.kernels.Fp8BlockWeight(w, gate_up=True) for w in w16]
+    x = torch.randn(rows, hidden, generator=g, device=dev).to(torch.bfloat16)
+    xq, xs = nqt.kernels.fp8_quantize_rows(x)
+    act = torch.empty(rows, ffn, dtype=torch.bfloat16, device=dev)
+    ws = nqt.kernels.fp8_gemm_workspace(dev, rows, 2 * ffn, hidden)
+
+    def fp8_pass():
+        for w in w8:
+            nqt.kernels.linear_fp8(xq, xs, w, out=act, workspace=ws)
+
+    def bf16_pass():
+        for w in w16:
+            nqt.kernels.silu_and_mul(torch.nn.functional.linear(x, w), out=act)
+
+    def graph_ms(fn) -> float:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(max(args.warmup, 1)):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        for _ in range(args.warmup):
+            gr.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+
+    lib_mod.reset_launch_count()
+    with ClockSampler(dev) as clocks:
+        fp8_ms = graph_ms(fp8_pass)
+    launches = lib_mod.launch_count()
+    bf16_ms = graph_ms(bf16_pass)
+    us = fp8_ms * 1e3 / layers
+    # algorithmic bytes of one call: e4m3 weights + block scales, e4m3 X + its scales, bf16 Y
+    nbytes = 2 * ffn * hidden + (2 * ffn // 128) * (hidden // 128) * 4 + rows * hidden + (hidden // 128) * rows * 4 \
+        + rows * ffn * 2
+    peak, peak_kind = peaks()
+    achieved = nbytes / (us * 1e-6) / 1e9
+    line = {
+        "metric": "talker FP8 gate/up GEMM time per call (M=64, N=12288, K=2048, SwiGLU fused)",
+        "value": us,
+        "unit": "us",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": fp8_ms,
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8 e4m3 (block-scaled, fp32 accumulate)",
+        "data": "synthetic (random-init bf16 weights quantised at load, N(0,1) rows)",
+        "config": {"workload": f"{layers} layers of talker gate/up weights called in turn from one CUDA graph "
+                               "(weights larger than L2)", "global_batch": rows * world, "seq_len": hidden,
+                   "parallelism": f"dp{world}", "gate_up": GATE_UP_NOTE["fp8"]},
+        "bf16_cublas_us_per_call": bf16_ms * 1e3 / layers,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "gemm_fp8_kernel", "bytes_per_launch": nbytes, "us_per_launch": us,
+                     "peak_source": f"{peak_kind} HBM copy (MEASURED_PEAKS.json hbm_gbs)"},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "device_status": nqt.kernels.read_status(dev),
+    }
+    if emit and rank == 0:
+        print(json.dumps(line), flush=True)
+    return line
+
+
 def run_sampler(args, world, rank, local) -> None:
     """The fused sampler's HBM roofline (SamplerWorkload) as its own bench line."""
 
@@ -773,6 +866,9 @@ def main() -> None:
     if args.workload == "serve":
         run_serve(args, world, rank, local)
         return
+    if args.workload == "gate_up":
+        run_gate_up(args, world, rank, local)
+        return
     nqt = importlib.import_module("nari-qwen3-tts_b200")
     from importlib import import_module
 
@@ -919,6 +1015,10 @@ def main() -> None:
         line["config4_mixed"] = _summary(run_mixed(sub, world, rank, local, emit=False))
         torch.cuda.empty_cache()
         line["config3_code_predictor"] = _summary(run_cp(sub, world, rank, local, emit=False))
+        torch.cuda.empty_cache()
+        gu = run_gate_up(sub, world, rank, local, emit=False)
+        line["gate_up_fp8_gemm"] = {"us_per_call": gu["value"], "bf16_cublas_us_per_call": gu["bf16_cublas_us_per_call"],
+                                    "roofline": gu["roofline"]}
         torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds, shape.num_layers)
