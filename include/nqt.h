@@ -46,6 +46,7 @@ extern "C" {
 #define NQT_DEV_BAD_SLOT 0x8      /* planner: request slot outside the table */
 #define NQT_DEV_TABLE_FULL 0x10   /* planner: a request outgrew its page-table row */
 #define NQT_DEV_CAPACITY 0x20     /* metadata outgrew a static buffer */
+#define NQT_DEV_BAD_TOKEN 0x40    /* a token id outside [0, vocab); its row is left unchanged */
 
 /* nqt_decode_attention_ex flags */
 #define NQT_DECODE_OVERLAP_KV_WRITE 0x1 /* see nqt_decode_attention_ex */
@@ -434,6 +435,20 @@ int nqt_gemm_pack_weight(const void* w, int64_t ldw, int n, int k, int interleav
                          void* stream);
 int nqt_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, void* y, int64_t ldy, const void* bias,
                   int m, int n, int k, int epilogue, int split, int32_t* status, void* stream);
+
+/*
+ * Code-predictor frame glue after codebook g's tokens are sampled, one launch for the six torch ops of the
+ * whole-frame loop (executor/code_predictor.py:160-235; the next step's input norm,
+ * model/components.py:254-258).  Per row: frames[row * frames_stride] = token;
+ * codec_sum[row] = bf16(codec_sum[row] + codec_emb[token]) (accumulate != 0) or codec_emb[token];
+ * when proj_emb is given, residual[row] = proj_emb[token] and h[row] = bf16(rmsnorm(residual[row]) * ln)
+ * (the nqt_rmsnorm arithmetic).  codec_emb [vocab, talker_hidden], proj_emb [vocab, hidden], rows
+ * contiguous, bf16, 16-byte aligned; hidden <= 4096.  Tokens outside [0, vocab) set NQT_DEV_BAD_TOKEN.
+ */
+int nqt_cp_codec_step(const int64_t* tokens, int rows, int64_t* frames, int64_t frames_stride,
+                      const void* codec_emb, int vocab, int talker_hidden, void* codec_sum, int accumulate,
+                      const void* proj_emb, const void* ln, int hidden, float eps, void* residual, void* h,
+                      int dtype, int32_t* status, void* stream);
 
 /*
  * FP8 (e4m3) block-scaled gate/up projection.  The reference's production

@@ -27,6 +27,7 @@ NQT_DEV_KV_EXHAUSTED = 0x4
 NQT_DEV_BAD_SLOT = 0x8
 NQT_DEV_TABLE_FULL = 0x10
 NQT_DEV_CAPACITY = 0x20
+NQT_DEV_BAD_TOKEN = 0x40
 
 NQT_BF16 = 0
 NQT_F16 = 1
@@ -96,6 +97,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqt_silu_and_mul": (I, [P, L, P, L, I, I, I, P]),
     "nqt_gemm_pack_weight": (I, [P, L, I, I, I, P, P]),
     "nqt_gemm_bf16": (I, [P, L, P, P, L, P, I, I, I, I, I, P, P]),
+    "nqt_cp_codec_step": (I, [P, I, P, L, P, I, I, P, I, P, P, I, F, P, P, I, P, P]),
     "nqt_fp8_quantize_weight_blocks": (I, [P, L, I, I, P, L, P, P]),
     "nqt_fp8_quantize_rows": (I, [P, L, I, I, P, L, P, L, P]),
     "nqt_fused_add_rmsnorm_fp8": (I, [P, P, P, I, I, F, P, L, P, L, I, I, P]),

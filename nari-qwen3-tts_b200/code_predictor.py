@@ -14,7 +14,9 @@ A depth step runs 5 decoder layers; each layer's attention is one fused launch
 (QK RMSNorm + RoPE, K/V write into the dense cache at the step's position,
 short-cache GQA attention: nqt_cp_decode_attention), the glue is the fused
 add + RMSNorm and SwiGLU kernels and the projections are cuBLAS calls.
-Weights are random (bf16).
+Between depth steps one launch (nqt_cp_codec_step) writes the frame's code,
+adds the codec embedding to the sum and prepares the next step's input and
+its first norm, in place of six torch / glue ops.  Weights are random (bf16).
 """
 
 from __future__ import annotations
@@ -97,6 +99,7 @@ class CodePredictorFrame:
         self.codec_sum = torch.zeros(rows, s.talker_hidden, dtype=bf16, device=dev)
         self._act = torch.empty(rows, s.ffn, dtype=bf16, device=dev)
         self._residual = torch.empty(rows, s.hidden, dtype=bf16, device=dev)
+        self._h = torch.empty(rows, s.hidden, dtype=bf16, device=dev)  # a depth step's first normed input
         self._token = torch.zeros(rows, dtype=torch.long, device=dev)
         # per-group logits stay resident (one [rows, vocab] slab per residual codebook)
         self.logits = torch.empty(s.groups - 1, rows, s.vocab, dtype=bf16, device=dev)
@@ -110,17 +113,21 @@ class CodePredictorFrame:
         groups = torch.arange(1, self.shape.groups, device=self.device)
         self.offsets.copy_((frame_index * FRAME_STRIDE + groups * CODEBOOK_STRIDE).unsqueeze(0).expand(self.rows, -1))
 
-    def _depth_step(self, x: torch.Tensor, cache_pos: int, final_norm: bool,
+    def _depth_step(self, x: torch.Tensor | None, cache_pos: int, final_norm: bool,
                     residuals: list | None = None) -> torch.Tensor:
-        """Five layers on one token per row at `cache_pos` (model/components.py:254-356).
+        """Five layers on one token per row at `cache_pos` (model/components.py:254-356).  ``x`` None: the
+        input is already in the residual buffer and its first norm in ``_h`` (written by cp_codec_step).
         ``residuals`` (parity tests) receives the residual stream before each layer and after the last."""
 
         s = self.shape
         hq, hkv, d = s.num_heads, s.num_kv_heads, s.head_dim
         rows = self.rows
         residual = self._residual
-        residual.copy_(x)
-        h = kernels.rmsnorm(x, self.ln_in[0], s.eps)
+        if x is None:
+            h = self._h
+        else:
+            residual.copy_(x)
+            h = kernels.rmsnorm(x, self.ln_in[0], s.eps, out=self._h)
         for layer in range(s.num_layers):
             if residuals is not None:
                 residuals.append(residual.clone())
@@ -161,22 +168,23 @@ class CodePredictorFrame:
         self._depth_step(hidden0, 0, final_norm=False, residuals=residuals)
         if trace is not None:
             trace.append((residuals, cache_before, None))
-        self.frames[:, 0].copy_(self.layer0_token)
-        self.codec_sum.copy_(F.embedding(self.layer0_token, self.layer0_embedding))
-        x = F.embedding(self.layer0_token, self.projected_layer0)
+        # codebook 0 (the talker's token): the frame's first code, the codec sum, the next step's input + norm
+        kernels.cp_codec_step(self.layer0_token, self.frames[:, 0], self.layer0_embedding, self.codec_sum,
+                              accumulate=False, proj_emb=self.projected_layer0, ln=self.ln_in[0], eps=s.eps,
+                              residual=self._residual, h=self._h)
         for group in range(1, s.groups):
             cache_before = self.kv_cache.clone() if trace is not None else None
             residuals = [] if trace is not None else None
-            hidden = self._depth_step(x, group, final_norm=True, residuals=residuals)
+            hidden = self._depth_step(None, group, final_norm=True, residuals=residuals)
             if trace is not None:
                 trace.append((residuals, cache_before, hidden.clone()))
             logits = torch.matmul(hidden, self.lm_head[group - 1].t(), out=self.logits[group - 1])
             sample_rows(logits, self.temperature, self.top_k, self.top_p, self.seed, self.offsets[:, group - 1],
                         round_scaled_to_input=False, out=self._token)
-            self.frames[:, group].copy_(self._token)
-            self.codec_sum.add_(F.embedding(self._token, self.codec_embedding[group - 1]))
-            if group < s.groups - 1:
-                x = F.embedding(self._token, self.projected_residual[group - 1])
+            last = group == s.groups - 1
+            kernels.cp_codec_step(self._token, self.frames[:, group], self.codec_embedding[group - 1], self.codec_sum,
+                                  proj_emb=None if last else self.projected_residual[group - 1], ln=self.ln_in[0],
+                                  eps=s.eps, residual=self._residual, h=self._h)
         return self.frames
 
     def capture(self, warmup: int = 2) -> None:

@@ -294,6 +294,7 @@ __all__ = [
     "Fp8BlockWeight",
     "PackedWeight",
     "clear_status",
+    "cp_codec_step",
     "cp_decode_attention_",
     "decode_attn_nhd_short_cache",
     "device_status",
@@ -406,6 +407,33 @@ def linear(x: torch.Tensor, weight: PackedWeight, bias: torch.Tensor | None = No
     call("nqt_gemm_bf16", ptr(x), x.stride(0), ptr(weight.data), ptr(out), out.stride(0), ptr(bias),
          m, weight.n, weight.k, epilogue, int(split), ptr(device_status(x.device)), _lib.stream_handle(x.device))
     return out
+
+
+def cp_codec_step(tokens: torch.Tensor, frames_col: torch.Tensor, codec_emb: torch.Tensor, codec_sum: torch.Tensor,
+                  *, accumulate: bool = True, proj_emb: torch.Tensor | None = None, ln: torch.Tensor | None = None,
+                  eps: float = 1e-6, residual: torch.Tensor | None = None, h: torch.Tensor | None = None) -> None:
+    """The code-predictor frame's glue after a codebook's tokens are sampled (executor/code_predictor.py:
+    160-235), one launch: frames_col <- tokens; codec_sum (+)= codec_emb[tokens]; with ``proj_emb``,
+    residual <- proj_emb[tokens] and h <- rmsnorm(residual) * ln (the next depth step's input)."""
+
+    rows = tokens.shape[0]
+    if tokens.dtype != torch.long or frames_col.dtype != torch.long or frames_col.shape[0] != rows:
+        raise TypeError("cp_codec_step takes int64 tokens and an int64 frames column")
+    if codec_emb.dtype != torch.bfloat16 or not codec_emb.is_contiguous() or not codec_sum.is_contiguous() \
+            or codec_sum.shape != (rows, codec_emb.shape[1]):
+        raise ValueError("cp_codec_step needs contiguous bf16 codec_emb [vocab, H] and codec_sum [rows, H]")
+    hidden = 0
+    if proj_emb is not None:
+        hidden = proj_emb.shape[1]
+        for t in (proj_emb, ln, residual, h):
+            if t is None or not t.is_contiguous() or t.dtype != torch.bfloat16:
+                raise ValueError("cp_codec_step needs contiguous bf16 proj_emb, ln, residual and h")
+        if residual.shape != (rows, hidden) or h.shape != (rows, hidden) or proj_emb.shape[0] != codec_emb.shape[0]:
+            raise ValueError("cp_codec_step: residual / h must be [rows, hidden] and the tables share the vocab")
+    call("nqt_cp_codec_step", ptr(tokens), rows, ptr(frames_col), frames_col.stride(0), ptr(codec_emb),
+         codec_emb.shape[0], codec_emb.shape[1], ptr(codec_sum), 1 if accumulate else 0, ptr(proj_emb), ptr(ln),
+         hidden, float(eps), ptr(residual), ptr(h), _lib.dtype_code(codec_emb.dtype), ptr(device_status(tokens.device)),
+         _lib.stream_handle(tokens.device))
 
 
 # ---------------------------------------------------------------- FP8 block-scaled gate/up

@@ -15,7 +15,9 @@ Sampling is discontinuous, so the frame is checked in parts:
   steps, and the codec embedding sum (bf16 gathers + adds) is bit-exact;
 * sampling: each GPU code is the fused sampler's draw on the GPU logits of
   its group (a replay of the same draw) and lies inside the reference's
-  filtered top-k support of those logits.
+  filtered top-k support of those logits;
+* the fused glue between depth steps (nqt_cp_codec_step) equals the six ops
+  it replaces bit for bit.
 """
 
 from __future__ import annotations
@@ -24,6 +26,7 @@ import importlib
 
 import pytest
 import torch
+import torch.nn.functional as F
 
 from oracle import sampler as osamp
 from oracle.code_predictor import CpuCodePredictorFrame
@@ -150,3 +153,40 @@ def test_graph_replay_and_host_step_reproduce_the_eager_frame(frame):
     torch.cuda.synchronize()
     assert not torch.equal(f.frames, codes)
     assert torch.equal(f.frames[:, 0], codes[:, 0])
+
+
+@pytest.mark.parametrize("accumulate,with_next", [(True, True), (False, True), (True, False)])
+def test_codec_step_equals_the_unfused_ops(nqt, cuda, accumulate, with_next):
+    """nqt_cp_codec_step against the six ops it replaces: the frame's code column, the codec embedding sum
+    (bf16 add), the next step's input and its rmsnorm - all bit for bit."""
+
+    g = torch.Generator(device=cuda).manual_seed(11)
+    rows, vocab, th, hd = 37, 2048, 2048, 1024
+    tokens = torch.randint(0, vocab, (rows,), generator=g, device=cuda)
+    emb = (0.5 * torch.randn(vocab, th, generator=g, device=cuda)).to(torch.bfloat16)
+    proj = torch.randn(vocab, hd, generator=g, device=cuda).to(torch.bfloat16)
+    ln = (1 + 0.1 * torch.randn(hd, generator=g, device=cuda)).to(torch.bfloat16)
+    sum0 = torch.randn(rows, th, generator=g, device=cuda).to(torch.bfloat16)
+    frames = torch.zeros(rows, 16, dtype=torch.long, device=cuda)
+    codec_sum, res, h = sum0.clone(), torch.zeros(rows, hd, dtype=torch.bfloat16, device=cuda), \
+        torch.zeros(rows, hd, dtype=torch.bfloat16, device=cuda)
+    nqt.kernels.cp_codec_step(tokens, frames[:, 5], emb, codec_sum, accumulate=accumulate,
+                              proj_emb=proj if with_next else None, ln=ln, eps=1e-6, residual=res, h=h)
+    torch.cuda.synchronize()
+    assert torch.equal(frames[:, 5], tokens) and int(frames[:, :5].abs().sum()) == 0
+    want_sum = sum0 + F.embedding(tokens, emb) if accumulate else F.embedding(tokens, emb)
+    assert torch.equal(codec_sum, want_sum)
+    if with_next:
+        x = F.embedding(tokens, proj)
+        assert torch.equal(res, x)
+        assert torch.equal(h, nqt.kernels.rmsnorm(x, ln, 1e-6))
+    # an id outside the vocabulary: status bit, the row left as it was
+    nqt.kernels.clear_status(cuda)
+    bad = tokens.clone()
+    bad[3] = vocab
+    before = codec_sum.clone()
+    nqt.kernels.cp_codec_step(bad, frames[:, 6], emb, codec_sum, proj_emb=None)
+    torch.cuda.synchronize()
+    assert nqt.kernels.read_status(cuda) & nqt._lib.NQT_DEV_BAD_TOKEN
+    assert torch.equal(codec_sum[3], before[3])
+    nqt.kernels.clear_status(cuda)
