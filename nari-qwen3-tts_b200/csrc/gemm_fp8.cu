@@ -95,12 +95,14 @@ struct Fp8Args {
   int epilogue, interleave;
   int stages, group, bufs;
   uint32_t tmem_cols;
+  int vec16;  // y 16-byte aligned with a row pitch of a multiple of 8: 16-byte stores
 };
 
 __host__ __device__ constexpr int x_bytes(int mp) { return mp * kBlockK; }
 // a stage: `group` W units [group][128 x 128 B] then their X slabs [group][mp x 128 B]
 __host__ __device__ constexpr int stage_bytes(int mp, int group) { return group * (kWBytes + x_bytes(mp)); }
-// the drained ring is reused by the split-K sum: two partials [mp][128] fp32 at least (the own one and a copy)
+// the drained ring is reused by the split-K sum (two partials [mp][128] fp32 at least: the own one and a copy)
+// and then by the staged output tile ([mp][128] bf16 at most)
 __host__ __device__ constexpr int ring_bytes(int mp, int group, int stages) {
   return stages * stage_bytes(mp, group) > mp * 1024 ? stages * stage_bytes(mp, group) : mp * 1024;
 }
@@ -379,33 +381,43 @@ __global__ void __launch_bounds__(kThreads, MINB)
     }
     if (last) {
       const int mt = a.m - t0 < MP ? a.m - t0 : MP;  // tokens of this chunk
-      const int64_t ldy = a.ldy;
+      // the output tile is staged in the drained ring as [MP tokens][cols] bf16, then leaves in 16-byte pieces
+      // of its token rows (scattered 2-byte stores from the owning threads cost several times more)
+      __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(smem);
+      const int cols = a.epilogue == kSiluMul ? 64 : kTileN;
       if (a.epilogue == kSiluMul) {
         // lane l < 16 holds a gate row and lane l + 16 the up row of the same output column: the gate lane
         // finishes tokens [0, MP/2), the up lane tokens [MP/2, MP), each sending the other the value it needs
         constexpr int kHalf = MP / 2;
         const bool gate = lane < 16;
-        const int col = tile * 64 + quarter * 16 + (lane & 15);
-        __nv_bfloat16* ycol = a.y + col;
-        // all outputs first (branch-free, so the iterations overlap), then the stores
-        __nv_bfloat16 out[kHalf];
+        const int c = quarter * 16 + (lane & 15);
+        const int tok0 = gate ? 0 : kHalf;
 #pragma unroll
         for (int e = 0; e < kHalf; ++e) {
           // gate lane sends gate[e + kHalf] and keeps gate[e]; up lane sends up[e] and keeps up[e + kHalf]
           const float other = __shfl_xor_sync(kFull, gate ? acc[e + kHalf] : acc[e], 16);
           const float g = gate ? acc[e] : other;
           const float u = gate ? other : acc[e + kHalf];
-          out[e] = __float2bfloat16_rn(silu_mul(bf16_round(g), bf16_round(u)));
+          stage[(tok0 + e) * 64 + c] = __float2bfloat16_rn(silu_mul(bf16_round(g), bf16_round(u)));
         }
-        const int tok0 = gate ? 0 : kHalf;
-#pragma unroll
-        for (int e = 0; e < kHalf; ++e)
-          if (tok0 + e < mt) ycol[static_cast<int64_t>(t0 + tok0 + e) * ldy] = out[e];
       } else {
-        __nv_bfloat16* ycol = a.y + tile * kTileN + row;
 #pragma unroll
-        for (int e = 0; e < MP; ++e)
-          if (e < mt) ycol[static_cast<int64_t>(t0 + e) * ldy] = __float2bfloat16_rn(acc[e]);
+        for (int e = 0; e < MP; ++e) stage[e * kTileN + row] = __float2bfloat16_rn(acc[e]);
+      }
+      epi_bar();
+      const int pieces = cols / 8;  // 16-byte pieces per token row
+      __nv_bfloat16* ybase = a.y + static_cast<int64_t>(t0) * a.ldy + tile * cols;
+      for (int idx = et; idx < mt * pieces; idx += 128) {
+        const int t = idx / pieces, pc = idx - t * pieces;
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + t * cols + pc * 8);
+        __nv_bfloat16* dst = ybase + static_cast<int64_t>(t) * a.ldy + pc * 8;
+        if (a.vec16) {
+          *reinterpret_cast<uint4*>(dst) = v;
+        } else {
+          const __nv_bfloat16* e8 = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) dst[j] = e8[j];
+        }
       }
     }
   }
@@ -679,7 +691,8 @@ extern "C" int nqt_gemm_fp8(const void* xq, int64_t ldxq, const float* xscale, i
             p.stages,
             p.group,
             p.bufs,
-            p.tmem_cols};
+            p.tmem_cols,
+            aligned(y, 16) && ldy % 8 == 0 ? 1 : 0};
   const dim3 grid(p.tiles, p.S, p.chunks);
   cudaError_t err;
   if (p.mp == 32)
