@@ -393,6 +393,8 @@ struct Lanes<__nv_bfloat16> {
     const unsigned short b = __bfloat16_as_ushort(__float2bfloat16_rn(t));
     return __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(t > 0.f ? b - 1 : b + 1)));
   }
+  // a bf16 value is exact in the top 16 bits of its fp32 pattern: bits 12-15 are zero
+  static constexpr uint32_t kExactLow = 0xFu;
 };
 
 template <>
@@ -422,6 +424,8 @@ struct Lanes<__half> {
     const unsigned short b = __half_as_ushort(__float2half_rn(t));
     return __half2float(__ushort_as_half(static_cast<unsigned short>(t > 0.f ? b - 1 : b + 1)));
   }
+  // an fp16 value converted to fp32 has its low 13 mantissa bits zero: bit 12 is zero
+  static constexpr uint32_t kExactLow = 0x1u;
 };
 
 template <>
@@ -448,6 +452,74 @@ struct Lanes<float> {
     return __uint_as_float(t > 0.f ? b - 1u : b + 1u);
   }
 };
+
+// ---- 32-bit rank keys (2-byte logits) ---------------------------------------
+// A candidate's key is the top 20 bits of the order key of its penalised value, then 4095 - token
+// (V <= 4096).  A bf16 or fp16 value converted to fp32 fits the 20 bits exactly, so for unpenalised
+// candidates equal keys mean equal values and the token breaks the tie as the reference does; a penalised
+// value that the 20 bits cut is moved one step towards its true position (it then keeps its order against
+// every exact key) and is marked inexact by its low bits.
+constexpr int kRankMaxVocab = 4096;
+constexpr int kRankCap = 192;  // candidates ranked: 128 at once, the rest merged into the top 64
+
+__device__ __forceinline__ uint32_t kmax(uint32_t a, uint32_t b) { return a > b ? a : b; }
+__device__ __forceinline__ uint32_t kmin(uint32_t a, uint32_t b) { return a < b ? a : b; }
+
+// Descending bitonic sort of the 32 E keys of a warp, key i = lane * E + e in slot e.  Every comparator
+// keeps the larger key at the lower index: merge kk opens with the flip comparator (i, i ^ (kk - 1)),
+// then half-cleaners at kk / 4 .. 1; distances below E stay inside a lane.
+template <int E>
+__device__ __forceinline__ void warp_sort_desc(uint32_t (&v)[E]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int kk = 2; kk <= 32 * E; kk <<= 1) {
+#pragma unroll
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      const bool flip = j == (kk >> 1);
+      const int d = flip ? kk - 1 : j;
+      if (d < E) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int f = e ^ d;
+          if (f > e) {
+            const uint32_t x = v[e], y = v[f];
+            v[e] = kmax(x, y);
+            v[f] = kmin(x, y);
+          }
+        }
+      } else {
+        // partner lane lane ^ (d / E); a flip comparator pairs slot e with the partner's slot E - 1 - e
+        const bool lower = (lane & (j / E)) == 0;
+        uint32_t pv[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) pv[e] = __shfl_xor_sync(kFull, v[flip ? E - 1 - e : e], d / E);
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = lower ? kmax(v[e], pv[e]) : kmin(v[e], pv[e]);
+      }
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ bool key_exact(uint32_t h) {  // h = 20-bit key part
+  const uint32_t bits = (h & 0x80000u) ? h : (~h & 0xFFFFFu);  // the value's own top 20 bits (sign aside)
+  return (bits & Lanes<T>::kExactLow) == 0u;
+}
+
+// the value whose 20-bit key part is h, exact when key_exact(h)
+__device__ __forceinline__ float key20_value(uint32_t h) {
+  return key_value((h << 12) | ((h & 0x80000u) ? 0u : 0xFFFu));
+}
+
+// key of a penalised value x of a 2-byte row (inexact only where `penalised`)
+template <typename T>
+__device__ __forceinline__ uint32_t rank_key(float x, bool pen_applied, int token) {
+  const uint32_t ok32 = order_key(x);
+  uint32_t h = ok32 >> 12;
+  const bool pos = (ok32 & 0x80000000u) != 0u;
+  if (pen_applied && key_exact<T>(h) && (ok32 & 0xFFFu) != (pos ? 0u : 0xFFFu)) h = pos ? (h | 1u) : (h & ~1u);
+  return (h << 12) | (4095u - static_cast<uint32_t>(token));
+}
 
 template <int G>
 struct FastShared {
@@ -704,6 +776,102 @@ __device__ bool fast_row(const SampleArgs& a, RowParams p, int row, int group, i
   }
   if (n_cand > kCandCap) return false;
   __syncwarp();
+
+  if constexpr (sizeof(T) == 2) {
+    if (!a.round_scaled && V <= kRankMaxVocab) {
+      // ---- rank C with 32-bit keys: one 128-key sort (4 keys per lane, rank r in lane r / 4, slot
+      // r % 4); candidates 128-191 replace ranks 64-127 and the top 64 is sorted again
+      if (n_cand > kRankCap) return false;
+      const uint8_t* srow = SEEN ? a.seen + row * a.seen_stride : nullptr;
+      uint32_t key[4];
+      auto load_keys = [&](int i0, int step, bool use) {
+        float x[4];
+        int tok[4];
+        uint8_t sb[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = i0 + e * step;
+          const bool in = use && i < n_cand;
+          x[e] = in ? fs.cx[i] : 0.f;
+          tok[e] = in ? fs.cid[i] : 0;
+          if constexpr (SEEN) sb[e] = in ? srow[tok[e]] : 0;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if constexpr (SEEN) {
+            if (__any_sync(kFull, sb[e] != 0)) x[e] = penalised(x[e], sb[e] != 0, p.pen);
+          }
+          if (use) key[e] = i0 + e * step < n_cand ? rank_key<T>(x[e], sb[e] != 0, tok[e]) : 0u;
+        }
+      };
+      load_keys(lane, 32, true);
+      warp_sort_desc<4>(key);
+      uint32_t key64 = __shfl_sync(kFull, key[0], 16);  // rank 64: the neighbour of rank 63 when k = 64
+      if (n_cand > 128) {
+        load_keys(128 + (lane - 16) * 4, 1, lane >= 16);
+        warp_sort_desc<4>(key);
+        key64 = kmax(key64, __shfl_sync(kFull, key[0], 16));  // the largest key left out
+      }
+      // ranks lane and lane + 32
+      uint32_t r0, r1;
+      {
+        uint32_t a0[4], a1[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          a0[e] = __shfl_sync(kFull, key[e], lane >> 2);
+          a1[e] = __shfl_sync(kFull, key[e], 8 + (lane >> 2));
+        }
+        const int slot = lane & 3;
+        r0 = slot == 0 ? a0[0] : (slot == 1 ? a0[1] : (slot == 2 ? a0[2] : a0[3]));
+        r1 = slot == 0 ? a1[0] : (slot == 1 ? a1[1] : (slot == 2 ? a1[2] : a1[3]));
+      }
+      // check: the k-th penalised value reaches tau0 (everything outside C lies below tau0)
+      {
+        const uint32_t hk = __shfl_sync(kFull, (k - 1) < 32 ? r0 : r1, (k - 1) & 31) >> 12;
+        const uint32_t ht = order_key(tau0) >> 12;
+        if (!(hk > ht || (hk == ht && key_exact<T>(hk)))) return false;
+      }
+      // y of ranks lane and lane + 32: exact from the key, or from the logit for a cut penalised value
+      auto exact_y = [&](uint32_t kk, int r) {
+        const uint32_t h = kk >> 12;
+        float x = key20_value(h);
+        if (SEEN && r <= k && kk != 0u && !key_exact<T>(h))
+          x = penalised(to_f32(lrow[4095u - (kk & 4095u)]), true, p.pen);
+        return greedy ? x : __fdiv_rn(x, p.temp);
+      };
+      const float y0 = exact_y(r0, lane), y1 = exact_y(r1, lane + 32);
+      // neighbouring ranks r, r + 1 (r < k) whose keys are within two steps and not both exact may order
+      // differently by (y desc, token asc), e.g. when the division by T rounds them to one value: the
+      // exact values decide, and a wrong key order sends the row to the general path
+      {
+        const uint32_t d0 = __shfl_down_sync(kFull, r0, 1), b0 = __shfl_sync(kFull, r1, 0);
+        const uint32_t d1 = __shfl_down_sync(kFull, r1, 1);
+        const float e0 = __shfl_down_sync(kFull, y0, 1), f0 = __shfl_sync(kFull, y1, 0);
+        const float e1 = __shfl_down_sync(kFull, y1, 1);
+        auto wrong_pair = [&](uint32_t kx, float yx, uint32_t ky, float yy, bool have_y) {
+          const uint32_t hx = kx >> 12, hy = ky >> 12;
+          if (hx - hy > 2u || (key_exact<T>(hx) && key_exact<T>(hy))) return false;
+          if (!have_y) return true;  // rank 64's exact value is not at hand
+          const uint32_t tx = 4095u - (kx & 4095u), ty = 4095u - (ky & 4095u);
+          return !(yx > yy || (yx == yy && tx < ty));
+        };
+        const bool wrong = (lane < k && wrong_pair(r0, y0, lane < 31 ? d0 : b0, lane < 31 ? e0 : f0, true)) ||
+                           (lane + 32 < k && wrong_pair(r1, y1, lane < 31 ? d1 : key64, e1, lane < 31));
+        if (__any_sync(kFull, wrong)) return false;
+      }
+      const int token = draw_top64(a, p, row, cand_word(order_key(y0), 4095 - static_cast<int>(r0 & 4095u)),
+                                   cand_word(order_key(y1), 4095 - static_cast<int>(r1 & 4095u)), n0, n1);
+      if (a.probs != nullptr) {
+        const int64_t pbase = static_cast<int64_t>(row) * V;
+        for (int r = k + lane; r < V; r += 32) {
+          a.probs[pbase + r] = 0.f;
+          a.ids[pbase + r] = -1;
+        }
+      }
+      if (lane == 0) finish_row(a, row, token);
+      return true;
+    }
+  }
 
   // ---- exact penalty on the candidates (slot s of lane l is candidate l + 32 s)
   constexpr int kSlots = kCandCap / 32;

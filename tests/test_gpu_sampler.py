@@ -28,11 +28,30 @@ def _to(c, cuda):
     )
 
 
-def _check_case(nqt, cuda, c):
+def _tie_explained(c, row, d, probs, ids, noise, token):
+    """A token that differs from the oracle's on a row with ties: the kept sets (top-k, then top-p) may
+    hold different members of a tie group, since torch orders tied values arbitrarily; the multisets of kept
+    values must agree and the kernel's token must win the race over its own ranks."""
+
+    scaled = osamp.scaled_rows(c["logits"][row: row + 1], c["temperature"][row: row + 1],
+                               None if c["repetition_penalty"] is None else c["repetition_penalty"][row: row + 1],
+                               None if c["seen_token_mask"] is None else c["seen_token_mask"][row: row + 1])[0]
+    k = d[0]
+    kept_k = ids[row, :k][probs[row, :k] > 0].long()
+    kept_o = d[2][d[1] > 0]
+    if not torch.equal(torch.sort(scaled[kept_k]).values, torch.sort(scaled[kept_o]).values):
+        return False
+    race = probs[row, :k] / noise[row, :k]
+    return int(ids[row, int(torch.argmax(race))]) == token
+
+
+def _check_case(nqt, cuda, c, kernel_dtype=None):
     """Kernel vs oracle on one case.  The oracle's Exp(1) noise belongs to
     torch.topk's rank positions; torch orders exactly tied values arbitrarily
     while the kernel ranks them by token id, so the noise is handed to the
-    kernel by token id (the identity permutation when the row has no ties)."""
+    kernel by token id (the identity permutation when the row has no ties).
+    With ``kernel_dtype`` the kernel reads the logits in that type (values the
+    type holds exactly) and computes in fp32 as the oracle does."""
 
     details = osamp.row_details(c["logits"], c["temperature"], c["top_k"], c["top_p"], c["seed"], c["offset"],
                                 repetition_penalty=c["repetition_penalty"], seen_token_mask=c["seen_token_mask"])
@@ -40,12 +59,17 @@ def _check_case(nqt, cuda, c):
                                repetition_penalty=c["repetition_penalty"], seen_token_mask=c["seen_token_mask"])
     rows, vocab = c["logits"].shape
     a = _to(c, cuda)
+    extra = {}
+    if kernel_dtype is not None:
+        assert torch.equal(c["logits"].to(kernel_dtype).float(), c["logits"])
+        a["logits"] = a["logits"].to(kernel_dtype)
+        extra["round_scaled_to_input"] = False
 
     def run(noise):
         return nqt.sample_rows(
             a["logits"], a["temperature"], a["top_k"], a["top_p"], a["seed"], a["offset"],
             repetition_penalty=a["repetition_penalty"], seen_token_mask=a["seen_token_mask"],
-            noise=noise.to(cuda), return_probs=True,
+            noise=noise.to(cuda), return_probs=True, **extra,
         )
 
     _, _, ids_k = run(torch.ones(rows, vocab))
@@ -61,11 +85,30 @@ def _check_case(nqt, cuda, c):
                 noise[row, r] = d[3][i]
     tokens, probs, ids = run(noise)
     torch.cuda.synchronize()
-    assert tokens.cpu().tolist() == want.tolist(), c.get("name")
+    if kernel_dtype is None:
+        assert tokens.cpu().tolist() == want.tolist(), c.get("name")
+    else:
+        # values of a 2-byte type tie: a differing token must be explained by the tie order
+        t_k = tokens.cpu()
+        for row in (t_k != want).nonzero().flatten().tolist():
+            assert details[row] is not None and _tie_explained(c, row, details[row], probs.cpu(), ids.cpu(),
+                                                                noise, int(t_k[row])), row
+    scaled_all = osamp.scaled_rows(c["logits"], c["temperature"], c["repetition_penalty"], c["seen_token_mask"]) \
+        if kernel_dtype is not None else None
     for row, d in enumerate(details):
         if d is None:
             continue
         k = d[0]
+        if kernel_dtype is not None:
+            # tie-agnostic: the ranked values equal the oracle's top-k values, ordered by (value desc, token
+            # asc), and the probabilities agree as multisets
+            sc, kid = scaled_all[row], ids[row, :k].cpu().long()
+            v = sc[kid]
+            assert torch.equal(v, torch.sort(sc[d[2]], descending=True).values), row
+            assert bool(((v[:-1] > v[1:]) | ((v[:-1] == v[1:]) & (kid[:-1] < kid[1:]))).all()), row
+            torch.testing.assert_close(torch.sort(probs[row, :k].cpu()).values, torch.sort(d[1]).values,
+                                       atol=PROB_ATOL, rtol=0)
+            continue
         got_ids = ids[row, :k].cpu().long()
         pos = {int(t): i for i, t in enumerate(d[2])}
         shared = [r for r in range(k) if int(got_ids[r]) in pos]
@@ -282,3 +325,122 @@ def test_warps_per_row_variants_match_oracle(nqt, cuda, rows):
     }
     c["temperature"][::11] = 0.0
     _check_case(nqt, cuda, c)
+
+
+# ---- 2-byte logits: 32-bit rank keys -------------------------------------------------------------
+# Rows of bf16 / fp16 logits whose y is not rounded to the logits type rank their candidates with 32-bit
+# keys (20-bit penalised value, 12-bit token); fp32 logits holding the same values take the 64-bit ranking.
+# Both compute in fp32, so the ranks must agree exactly.
+
+
+def _mixed_case(g, rows, vocab, dtype=torch.bfloat16):
+    """Rows of every kind the fast paths meet: plain penalised rows (the stacked-step workload), greedy,
+    k = 1 / 17 / 64 / 65 / 0, top-p off and 0.5, penalty below one and 1.5, masked vocab, ties, a dominant
+    logit, NaN and +inf."""
+
+    logits = (torch.randn(rows, vocab, generator=g) * 2.0)
+    kind = torch.arange(rows) % 16
+    logits[kind == 8, : vocab // 3] = float("-inf")
+    logits[kind == 9] = logits[kind == 9].mul(0.75).round()
+    logits[kind == 10, 11] += 30.0
+    logits[kind == 6, 5] = float("nan")
+    logits[kind == 7, 9] = float("inf")
+    temperature = torch.full((rows,), 0.9)
+    temperature[kind == 0] = 0.0
+    temperature[kind == 12] = 1.7
+    top_k = torch.full((rows,), 50, dtype=torch.int32)
+    top_k[kind == 1] = 64
+    top_k[kind == 2] = 65
+    top_k[kind == 3] = 0
+    top_k[kind == 11] = 1
+    top_k[kind == 13] = 17
+    top_p = torch.full((rows,), 0.95)
+    top_p[kind == 4] = 1.0
+    top_p[kind == 14] = 0.5
+    penalty = torch.full((rows,), 1.05)
+    penalty[kind == 5] = 0.8
+    penalty[kind == 15] = 1.5
+    return {
+        "logits": logits.to(dtype),
+        "temperature": temperature,
+        "top_k": top_k,
+        "top_p": top_p,
+        "seed": torch.randint(0, 2**62, (rows,), generator=g),
+        "offset": torch.randint(0, 2**40, (rows,), generator=g),
+        "repetition_penalty": penalty,
+        "seen_token_mask": torch.rand(rows, vocab, generator=g) < 0.02,
+    }
+
+
+def _sample(nqt, a, sl=slice(None), noise=None, probs=False):
+    return nqt.sample_rows(
+        a["logits"][sl], a["temperature"][sl], a["top_k"][sl], a["top_p"][sl], a["seed"][sl], a["offset"][sl],
+        repetition_penalty=None if a["repetition_penalty"] is None else a["repetition_penalty"][sl],
+        seen_token_mask=None if a["seen_token_mask"] is None else a["seen_token_mask"][sl],
+        round_scaled_to_input=False, noise=None if noise is None else noise[sl], return_probs=probs)
+
+
+@pytest.mark.parametrize("rows", [64, 2048])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("with_seen", [True, False])
+def test_rank_keys_match_the_64_bit_ranking(nqt, cuda, rows, dtype, with_seen):
+    """The same values as 2-byte and as fp32 logits: identical ranks (token ids in rank order), the
+    probabilities within 1e-6, and the same draws, both from the production Philox stream and from the
+    noise entry, except where two ranks' p / E agree to rounding (the softmax sums in another order)."""
+
+    g = torch.Generator().manual_seed(rows + int(with_seen) + (7 if dtype == torch.float16 else 0))
+    c = _mixed_case(g, rows, 3072, dtype)
+    if not with_seen:
+        c["repetition_penalty"] = c["seen_token_mask"] = None
+    a = {k: (v.to(cuda) if v is not None else None) for k, v in c.items()}
+    f = dict(a, logits=a["logits"].float())
+    t2, tf = _sample(nqt, a), _sample(nqt, f)
+    torch.cuda.synchronize()
+    assert int((t2 != tf).sum()) <= 2
+    noise = torch.empty(rows, 3072).exponential_(generator=g).to(cuda)
+    t1, p1, i1 = _sample(nqt, a, noise=noise, probs=True)
+    t2, p2, i2 = _sample(nqt, f, noise=noise, probs=True)
+    torch.cuda.synchronize()
+    assert torch.equal(i1, i2)
+    torch.testing.assert_close(p1, p2, atol=1e-6, rtol=0, equal_nan=True)  # NaN rows: NaN on both
+    for row in (t1 != t2).nonzero().flatten().tolist():
+        r1 = int((i1[row] == t1[row]).nonzero()[0])
+        r2 = int((i1[row] == t2[row]).nonzero()[0])
+        s1 = float(p1[row, r1] / noise[row, r1])
+        s2 = float(p1[row, r2] / noise[row, r2])
+        assert abs(s1 - s2) <= 1e-6 * max(s1, s2), (row, s1, s2)
+
+
+def test_bf16_rows_match_oracle(nqt, cuda):
+    g = torch.Generator().manual_seed(33)
+    rows = 2048
+    c = _mixed_case(g, rows, 3072)
+    # finite rows without whole tie groups: torch.topk keeps an arbitrary part of a tie group at the k-th
+    # value, so NaN / +inf rows and integer-valued rows are covered against the 64-bit ranking above
+    kind = torch.arange(rows) % 16
+    redo = (kind == 6) | (kind == 7) | (kind == 9)
+    c["logits"][redo] = (torch.randn(int(redo.sum()), 3072, generator=g) * 2.0).to(torch.bfloat16)
+    c["logits"] = c["logits"].float()  # bf16 values: the oracle computes on them in fp32, the kernel reads bf16
+    _check_case(nqt, cuda, c, kernel_dtype=torch.bfloat16)
+
+
+def test_rank_keys_on_unaligned_rows_and_seen_update(nqt, cuda):
+    # rows that do not start on 16 bytes take the general path; update_seen marks each drawn token once
+    g = torch.Generator().manual_seed(44)
+    rows = 512
+    c = _mixed_case(g, rows, 3072)
+    a = {k: v.to(cuda) for k, v in c.items()}
+    wide = torch.full((rows, 3080), float("-inf"), dtype=torch.bfloat16, device=cuda)
+    wide[:, 4:3076] = a["logits"]
+    t_shift = _sample(nqt, dict(a, logits=wide[:, 4:3076]))
+    t_plain = _sample(nqt, a)
+    assert torch.equal(t_shift, t_plain)
+    seen = a["seen_token_mask"].clone()
+    tokens = nqt.sample_rows(a["logits"], a["temperature"], a["top_k"], a["top_p"], a["seed"], a["offset"],
+                             repetition_penalty=a["repetition_penalty"], seen_token_mask=seen, update_seen=True,
+                             round_scaled_to_input=False)
+    torch.cuda.synchronize()
+    assert torch.equal(tokens, t_plain)
+    idx = torch.arange(rows, device=cuda)
+    assert bool(seen[idx, tokens].all())
+    assert int(seen.ne(a["seen_token_mask"]).sum()) == int((~a["seen_token_mask"][idx, tokens]).sum())
