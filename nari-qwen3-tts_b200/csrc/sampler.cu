@@ -395,6 +395,15 @@ struct Lanes<__nv_bfloat16> {
   }
   // a bf16 value is exact in the top 16 bits of its fp32 pattern: bits 12-15 are zero
   static constexpr uint32_t kExactLow = 0xFu;
+  // 16-bit order key of a bf16 value held in a float (larger value, larger key) and its inverse
+  static __device__ __forceinline__ uint32_t key16(float v) {
+    const uint32_t b = __float_as_uint(v) >> 16;
+    return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  }
+  static __device__ __forceinline__ float value16(uint32_t k) {
+    const uint32_t b = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
+    return __uint_as_float(b << 16);
+  }
 };
 
 template <>
@@ -426,6 +435,15 @@ struct Lanes<__half> {
   }
   // an fp16 value converted to fp32 has its low 13 mantissa bits zero: bit 12 is zero
   static constexpr uint32_t kExactLow = 0x1u;
+  // 16-bit order key of an fp16 value held in a float (larger value, larger key) and its inverse
+  static __device__ __forceinline__ uint32_t key16(float v) {
+    const uint32_t b = __half_as_ushort(__float2half_rn(v));
+    return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  }
+  static __device__ __forceinline__ float value16(uint32_t k) {
+    const uint32_t b = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(b)));
+  }
 };
 
 template <>
@@ -706,8 +724,23 @@ __device__ bool fast_row(const SampleArgs& a, RowParams p, int row, int group, i
   // ---- cut 1: tau0 = k-th largest chunk maximum (every warp of the group sorts the same 64 values)
   const bool odd = (c0 != c0) || (c1 != c1) || c0 == __builtin_huge_valf() || c1 == __builtin_huge_valf();
   if (__any_sync(kFull, odd)) return false;  // NaN or +inf: the general path handles them
-  warp_sort64_desc_f32(c0, c1);
-  const float tau0 = rank_value(c0, c1, k - 1);
+  float tau0;
+  if constexpr (sizeof(T) == 2) {
+    // the chunk maxima are exact 2-byte values: bisection on their 16-bit order keys, counting the keys at
+    // or above each candidate over the warp; the result is the largest key with at least k keys >= it
+    const uint32_t k0 = L::key16(c0), k1 = L::key16(c1);
+    uint32_t prefix = 0u;
+#pragma unroll
+    for (int bit = 15; bit >= 0; --bit) {
+      const uint32_t cand = prefix | (1u << bit);
+      const int cnt = static_cast<int>(__reduce_add_sync(kFull, (k0 >= cand ? 1u : 0u) + (k1 >= cand ? 1u : 0u)));
+      if (cnt >= k) prefix = cand;
+    }
+    tau0 = L::value16(prefix);
+  } else {
+    warp_sort64_desc_f32(c0, c1);
+    tau0 = rank_value(c0, c1, k - 1);
+  }
   if (!(tau0 > -__builtin_huge_valf())) return false;
   const uint32_t tau2 = L::splat(tau0);
   // the candidates' seen-mask bytes come from L2 later: start pulling the row's lines in now
