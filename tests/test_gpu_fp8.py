@@ -118,6 +118,7 @@ def _operands(m: int, n: int, k: int, seed: int):
     (100, 256, 1024, 4), (128, 512, 2048, 0), (130, 256, 512, 0), (300, 384, 1280, 0), (64, 1024, 2048, 0x401),
     (64, 1024, 2048, 0x201), (32, 2048, 2048, 0x308),
     (64, 12288, 2048, 0), (20, 12288, 2048, 0),  # 96 tiles: K split over 3 CTAs, two CTAs per SM
+    (1000, 512, 2048, 0),  # prefill-scale rows (the mixed batch with the FP8 gate/up): many token chunks
 ])
 def test_gemm_plain_matches_the_blockscaled_oracle(nqt, cuda, m, n, k, split):
     x, w = _operands(m, n, k, m * 7 + n)
@@ -132,7 +133,7 @@ def test_gemm_plain_matches_the_blockscaled_oracle(nqt, cuda, m, n, k, split):
     _check(y, want, 2.0 ** -7, f"m={m} n={n} k={k} split={split:#x}", 0.97)
 
 
-@pytest.mark.parametrize("m,split", [(64, 0), (64, 2), (7, 0), (200, 0)])
+@pytest.mark.parametrize("m,split", [(64, 0), (64, 2), (7, 0), (200, 0), (1000, 0)])
 def test_gemm_swiglu_matches_the_oracle(nqt, cuda, m, split):
     ffn, hidden = 1536, 2048
     x, w = _operands(m, 2 * ffn, hidden, 100 + m)
