@@ -320,10 +320,14 @@ __device__ __forceinline__ void finish_row(const SampleArgs& a, int row, int tok
 //           maximum: the k chunks whose maxima reach tau0 hold at least k elements >= tau0, so the
 //           raw top-k lies in C = {x >= tau0}.  A repetition penalty >= 1 only lowers a logit, so C
 //           also holds the top-k of the penalised row whenever the check below passes.  The maxima
-//           come from packed (x2) NaN-propagating max instructions on the raw vectors.
+//           come from packed (x2) NaN-propagating max instructions on the raw vectors; for 2-byte
+//           logits tau0 is found by bisection on their 16-bit order keys, else by a warp sort.
 //   prefilter  A vector whose packed maximum is below tau0 holds no candidate; the others (about
 //           a quarter) are copied to shared memory, then expanded element by element with warp
 //           ballots into C (at most 256).
+//   rank    2-byte logits whose y is not rounded to the logits type: all of C (at most 192) is ranked
+//           with 32-bit keys in one warp sort (the ranking block in fast_row has its checks); the steps below
+//           are the path of fp32 and y-rounded rows.
 //   exact   Only the candidates read their seen-mask byte and take the exact penalty; when C has
 //           more than 64, tau1 = the k-th largest of the 64 lane-local top-2 values narrows it to
 //           F = {x_pen >= tau1} (at least k), else F = C.  y = x_pen / T for F only; F is sorted in
